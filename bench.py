@@ -1,0 +1,416 @@
+#!/usr/bin/env python3
+"""MoE-block benchmark: Qwen3-30B-A3B-shaped 4-bit MoE layer decode on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl ours|reference]
+
+A step is one MoE-block forward (router + cache bias -> top-k -> dispatch ->
+4-bit SwiGLU experts -> combine) of one layer over a decode batch of T tokens
+(default 64; the workload also sweeps T = 1 and 8). Layers rotate over
+--layers distinct weight sets (48 x 340 MB = 16.3 GB, far above the 126 MB
+L2), each with its own seeded input batch, so no step reads weights another
+recent step left in L2. Inputs are synthetic and seeded: experts fp16
+N(0, 0.02) quantised to MLX affine 4-bit (group 64), router bf16 N(0, 0.02),
+activations bf16 N(0, 1), routing bias +0.5 on a seeded 25% expert subset.
+
+Prints one JSON line (rank 0). `value` = tokens/s with inputs resident in HBM
+(CUDA graphs of the C-ABI call, CUDA events); `e2e` = tokens/s through the
+public C-ABI call with pinned host buffers, host->device inputs and
+device->host output inside the timed region; `roofline` = the dominant
+kernel's algorithmic bytes per launch / its CUDA-event duration against the
+measured HBM copy bandwidth; `cpu_baseline` = the C restatement of the block
+timed on this host's cores.
+
+--impl reference times the reference's algorithm on the host cores (the C
+restatement in oracle/; the reference's own MLX path cannot run on Linux x86
+here) on the same workload and prints the same line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "MoE-layer decode tokens/s (Qwen3-30B-A3B-shaped 4-bit layer)"
+UNIT = "tokens/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--sweep", default="1,8", help="extra decode batch sizes to time")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------------- #
+# helpers
+# --------------------------------------------------------------------------- #
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons, sampled every 100 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def stop(self):
+        out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        if self.proc is None:
+            return out
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return out
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        out.update(sm_mhz=statistics.median(sm) if sm else None,
+                   sm_max_mhz=max(mx) if mx else None, reasons=reasons, samples=len(rows),
+                   power_w_max=max(float(r[3]) for r in rows
+                                   if r[3].replace(".", "").isdigit()) if rows else None)
+        return out
+
+
+def block_bytes(cfg, T, U):
+    """Algorithmic HBM bytes of one MoE-block step: the packed bytes of the
+    distinct experts selected, logits, x, out and the bias vector."""
+    return (U * cfg.bytes_per_expert + T * cfg.num_experts * 2 + T * cfg.hidden * 2 * 2
+            + cfg.num_experts * 4)
+
+
+def kernel_bytes(cfg, T, U):
+    """Algorithmic bytes per launch of each kernel of the block."""
+    D, I, E, k = cfg.hidden, cfg.inter, cfg.num_experts, cfg.top_k
+    P = T * k
+    return {
+        "route": T * E * 2 + E * 4 + T * D * 2 * 2 + T * (D // 64) * 4 + T * k * 8,
+        "dispatch": 2 * T * k * 4 + E * 16,
+        "gateup": U * 2 * D * I * 9 // 16 + T * D * 2 + P * I * 4,
+        "down": U * D * I * 9 // 16 + P * I * 4 + P * D * 4,
+        "combine": P * D * 4 + T * D * 2 + T * k * 8,
+    }
+
+
+KERNELS = ["route", "dispatch", "gateup", "down", "combine"]
+
+
+# --------------------------------------------------------------------------- #
+# CPU baseline (oracle C restatement)
+# --------------------------------------------------------------------------- #
+
+def cpu_baseline(cfg, T, seconds, layer_np=None, seed=0):
+    import numpy as np
+    from expert_sniper_b200.quant import cache_bias_vector, synthetic_inputs, synthetic_layer
+    from oracle import c_oracle
+    c_oracle.build()
+    if layer_np is None:
+        lay = synthetic_layer(cfg, seed=1000)
+        layer_np = {k: v.numpy() for k, v in lay.items()}
+    x, _, logits, _ = synthetic_inputs(cfg, T, seed=seed)
+    xf = x.float().numpy()
+    lf = logits.float().numpy()
+    bias = cache_bias_vector(cfg.num_experts, 0.5, 0)[0].numpy()
+    cores = os.cpu_count() or 1
+    times = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end or len(times) < 2:
+        t0 = time.perf_counter()
+        idx, w = c_oracle.route(lf, bias, cfg.top_k, cfg.norm_topk_prob)
+        c_oracle.expert_ffn(xf, layer_np, idx, w, nthreads=cores)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": T / med, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{len(times)} calls of one {cfg.name} layer at T={T} "
+                      f"(router + experts + combine), median {med * 1e3:.1f} ms/call"}
+
+
+# --------------------------------------------------------------------------- #
+# our arm, one GPU
+# --------------------------------------------------------------------------- #
+
+def run_ours_single(args):
+    import torch
+    from expert_sniper_b200 import MoEBlock, PRESETS, prepare_packed
+    from expert_sniper_b200.quant import cache_bias_vector, synthetic_inputs, synthetic_layer
+
+    cfg = PRESETS["qwen3-30b-a3b"]
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    T, L = args.tokens, args.layers
+    sweep = [int(s) for s in args.sweep.split(",") if s.strip() and int(s) != T]
+    t_setup = time.time()
+    packed = []
+    cpu_layer = None
+    for l in range(L):
+        lay = synthetic_layer(cfg, seed=1000 + l, device=dev)
+        packed.append(prepare_packed(cfg, lay))
+        if l == 0 and not args.no_cpu_baseline:
+            cpu_layer = {k: v.cpu().numpy() for k, v in lay.items()}
+        del lay
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    setup_s = time.time() - t_setup
+    bias = cache_bias_vector(cfg.num_experts, 0.5, 0)[0].to(dev)
+    Tmax = max([T] + sweep)
+    blocks = [MoEBlock(cfg, packed=p, max_tokens=Tmax) for p in packed]
+    stream = torch.cuda.Stream(dev)
+    peak, peak_kind = measured_peaks()
+
+    def make_case(Tc, seed_base):
+        xs, lgs, outs, U = [], [], [], []
+        for l in range(L):
+            x, _, lg, _ = synthetic_inputs(cfg, Tc, seed=seed_base + l, device=dev)
+            xs.append(x)
+            lgs.append(lg)
+            outs.append(torch.empty((Tc, cfg.hidden), dtype=torch.bfloat16, device=dev))
+            idx, _ = blocks[l].route(lg, bias)
+            U.append(int(torch.unique(idx).numel()))
+        return xs, lgs, outs, U
+
+    def capture(xs, lgs, outs, events=None):
+        graphs = []
+        with torch.cuda.stream(stream):
+            for l in range(L):
+                blocks[l].forward(xs[l], lgs[l], bias, out=outs[l])
+            torch.cuda.synchronize()
+            for l in range(L):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    if events is None:
+                        blocks[l].forward(xs[l], lgs[l], bias, out=outs[l])
+                    else:
+                        blocks[l].forward_timed(xs[l], lgs[l], bias, events[l], outs[l])
+                graphs.append(g)
+        torch.cuda.synchronize()
+        return graphs
+
+    def time_graphs(graphs, K, W):
+        with torch.cuda.stream(stream):
+            for s in range(W):
+                graphs[s % L].replay()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for s in range(W, W + K):
+                graphs[s % L].replay()
+            e1.record(stream)
+            e1.synchronize()
+        return e0.elapsed_time(e1) / K
+
+    def profile_kernels(xs, lgs, outs, K):
+        events = []
+        for l in range(L):
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+            for e in evs:
+                e.record(stream)  # creates the underlying cudaEvent_t
+            events.append(evs)
+        torch.cuda.synchronize()
+        graphs = capture(xs, lgs, outs, events)
+        tot = {k: [] for k in KERNELS}
+        done = 0
+        with torch.cuda.stream(stream):
+            while done < K:
+                n = min(L, K - done)
+                for l in range(n):
+                    graphs[l].replay()
+                torch.cuda.synchronize()
+                for l in range(n):
+                    evs = events[l]
+                    for i, name in enumerate(KERNELS):
+                        tot[name].append((l, evs[i].elapsed_time(evs[i + 1])))
+                done += n
+        del graphs
+        return tot
+
+    results = {}
+    for Tc in [T] + sweep:
+        xs, lgs, outs, U = make_case(Tc, seed_base=10_000 * Tc)
+        graphs = capture(xs, lgs, outs)
+        K = args.steps if Tc == T else min(args.steps, 4000)
+        W = max(3, args.warmup)
+        clocks = ClockSampler(0).start() if Tc == T else None
+        if clocks:
+            time.sleep(0.3)
+        ms = time_graphs(graphs, K, W)
+        clk = clocks.stop() if clocks else None
+        del graphs
+        mean_bytes = sum(block_bytes(cfg, Tc, U[s % L]) for s in range(W, W + K)) / K
+        prof = profile_kernels(xs, lgs, outs, min(K, 4 * L))
+        kmean = {k: statistics.mean(v for _, v in prof[k]) for k in KERNELS}
+        kb = {k: statistics.mean(kernel_bytes(cfg, Tc, U[l])[k] for l, _ in prof[k]) for k in KERNELS}
+        results[Tc] = dict(ms=ms, bytes=mean_bytes, U=statistics.mean(U), kmean=kmean, kb=kb,
+                           clocks=clk, xs=xs, lgs=lgs, outs=outs)
+
+    # e2e through the public API with host buffers
+    r = results[T]
+    xs_h = [x.cpu().pin_memory() for x in r["xs"]]
+    lg_h = [g.cpu().pin_memory() for g in r["lgs"]]
+    out_h = torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(r["xs"][0])
+    ld = torch.empty_like(r["lgs"][0])
+    od = torch.empty((T, cfg.hidden), dtype=torch.bfloat16, device=dev)
+    K_e2e = min(args.steps, 2000)
+    with torch.cuda.stream(stream):
+        def e2e_step(s):
+            l = s % L
+            xd.copy_(xs_h[l], non_blocking=True)
+            ld.copy_(lg_h[l], non_blocking=True)
+            blocks[l].forward(xd, ld, bias, out=od)
+            out_h.copy_(od, non_blocking=True)
+        for s in range(max(3, args.warmup)):
+            e2e_step(s)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for s in range(K_e2e):
+            e2e_step(s)
+        e1.record(stream)
+        e1.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / K_e2e
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = cpu_baseline(cfg, T, args.cpu_seconds, cpu_layer)
+
+    dom = max(KERNELS, key=lambda k: r["kmean"][k])
+    achieved = r["kb"][dom] / (r["kmean"][dom] * 1e-3) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            tj = json.load(f)
+        traffic = tj.get(f"{cfg.name}:T{T}:{dom}")
+    line = {
+        "metric": METRIC, "value": T / (r["ms"] * 1e-3), "unit": UNIT, "n_gpus": 1,
+        "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": r["ms"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4xbf16->f32",
+        "data": "synthetic (seeded; random-init 4-bit MLX-affine experts)",
+        "config": {"workload": f"{cfg.name} MoE layer decode, batch {T} tokens, routing bias +0.5 "
+                               f"on 25% cached experts, {L} rotating layers",
+                   "model": cfg.name, "hidden": cfg.hidden, "experts": cfg.num_experts,
+                   "top_k": cfg.top_k, "inter": cfg.inter, "tokens": T, "layers_rotated": L,
+                   "l2": f"working set {L} layers x {cfg.packed_bytes / 1e6:.0f} MB > L2",
+                   "parallelism": "single GPU"},
+        "gbs": r["bytes"] / (r["ms"] * 1e-3) / 1e9,
+        "block_roofline": {"bound": "hbm", "achieved": r["bytes"] / (r["ms"] * 1e-3) / 1e9,
+                           "peak": peak, "unit": "GB/s",
+                           "frac": r["bytes"] / (r["ms"] * 1e-3) / 1e9 / peak,
+                           "bytes_per_step": r["bytes"], "mean_distinct_experts": r["U"]},
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "algorithmic_bytes_per_launch": r["kb"][dom],
+                     "launch_ms": r["kmean"][dom]},
+        "kernel_ms": r["kmean"],
+        "e2e": {"value": T / (e2e_ms * 1e-3), "unit": UNIT,
+                "h2d_bytes_per_step": T * cfg.hidden * 2 + T * cfg.num_experts * 2,
+                "d2h_bytes_per_step": T * cfg.hidden * 2, "ms_per_step": e2e_ms},
+        "gpu_launches": 5 * args.steps,
+        "clocks": r["clocks"],
+        "cpu_baseline": cpu,
+        "sweep": [{"tokens": Tc, "ms_per_step": results[Tc]["ms"],
+                   "value": Tc / (results[Tc]["ms"] * 1e-3),
+                   "gbs": results[Tc]["bytes"] / (results[Tc]["ms"] * 1e-3) / 1e9,
+                   "frac": results[Tc]["bytes"] / (results[Tc]["ms"] * 1e-3) / 1e9 / peak,
+                   "kernel_ms": results[Tc]["kmean"]} for Tc in sweep],
+        "setup_s": setup_s,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_reference(args):
+    """The reference's algorithm on the host cores: oracle C restatement."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from expert_sniper_b200 import PRESETS
+    cfg = PRESETS["qwen3-30b-a3b"]
+    T = args.tokens
+    per_step = max(1.0, min(10.0, 60.0 / max(1, args.steps + args.warmup)))
+    base = cpu_baseline(cfg, T, per_step * (args.steps + args.warmup))
+    ms = T / base["value"] * 1e3
+    line = {
+        "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+        "data": "synthetic (seeded)",
+        "config": {"workload": f"{cfg.name} MoE layer decode, batch {T} tokens, routing bias +0.5",
+                   "model": cfg.name, "tokens": T},
+        "cpu_baseline": base,
+        "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "C restatement of generate.py:122-136 + engine.py:15-42 on the host cores "
+                "(MLX, the reference's own backend, is not installable on Linux x86)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.gpus > 1 or world > 1:
+        from expert_sniper_b200 import ep_bench
+        ep_bench.run(args)
+        return
+    run_ours_single(args)
+
+
+if __name__ == "__main__":
+    main()

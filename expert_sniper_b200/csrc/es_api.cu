@@ -1,0 +1,259 @@
+// C ABI of the MoE block (include/es_moe.h): argument checks, workspace
+// carving and kernel launches. No allocation, no host synchronisation except
+// in es_moe_read_error.
+#include <cuda_runtime.h>
+
+#include "es_kernels.cuh"
+#include "es_moe.h"
+
+namespace {
+
+using es::Workspace;
+
+es_status check_cfg(const es_moe_cfg* c) {
+  if (!c) return ES_ERR_INVALID_ARG;
+  if (c->group_size != 64 || c->bits != 4) return ES_ERR_UNSUPPORTED;
+  if (c->hidden <= 0 || c->inter <= 0 || c->num_experts <= 0 || c->top_k <= 0)
+    return ES_ERR_INVALID_ARG;
+  // gate/up CTAs give each warp 4 groups of D; down warps hold I/64 tiles
+  if (c->hidden % 256 || c->hidden > 4096) return ES_ERR_UNSUPPORTED;
+  const int kg = c->inter / 64;
+  if (c->inter % 64 || !(kg == 4 || kg == 8 || kg == 12 || kg == 16 || kg == 24 || kg == 32))
+    return ES_ERR_UNSUPPORTED;
+  if (c->num_experts > es::kMaxExperts) return ES_ERR_UNSUPPORTED;
+  if (c->top_k > es::kMaxTopK || c->top_k > c->num_experts) return ES_ERR_UNSUPPORTED;
+  if (c->shared_inter != 0 && c->shared_inter != c->inter) return ES_ERR_UNSUPPORTED;
+  return ES_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+es_status cuda_status(cudaError_t e) { return e == cudaSuccess ? ES_OK : ES_ERR_CUDA; }
+
+// Optional per-kernel instrumentation: events[i] is recorded before kernel i
+// (router, dispatch, gate/up, down, combine) and events[5] after the last.
+struct Marks {
+  void* const* ev = nullptr;
+  cudaError_t mark(int i, cudaStream_t st) const {
+    if (!ev) return cudaSuccess;
+    // under stream capture the record must become an event-record node of
+    // the graph (cudaEventRecordExternal), so it fires on every replay
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(st, &cs);
+    if (e != cudaSuccess) return e;
+    cudaEvent_t h = static_cast<cudaEvent_t>(ev[i]);
+    return cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(h, st, cudaEventRecordExternal)
+                                               : cudaEventRecord(h, st);
+  }
+};
+
+// Shared tail of es_moe_forward / es_moe_expert_ffn: dispatch, FFN, combine.
+es_status run_ffn(const es_moe_cfg* cfg, const Workspace& w, const int32_t* idx,
+                  const float* wts, const void* packed, void* out, int out_f32,
+                  int T, cudaStream_t st, const Marks& mk = Marks()) {
+  const int E = cfg->num_experts, k = cfg->top_k;
+  const int has_shared = cfg->shared_inter > 0;
+  es::DispatchArgs d{};
+  d.bitmap = w.bitmap; d.idx = idx; d.T = T; d.E = E; d.k = k;
+  d.has_shared = has_shared; d.W = w.W; d.wpre = w.wpre; d.n_active = w.n_active;
+  d.act_e = w.act_e; d.act_off = w.act_off; d.act_n = w.act_n;
+  d.pair_tok = w.pair_tok; d.pos = w.pos;
+  if (mk.mark(1, st) != cudaSuccess) return ES_ERR_CUDA;
+  cudaError_t ce = es::launch_dispatch(d, st);
+  if (ce != cudaSuccess) return ES_ERR_CUDA;
+
+  const long long routed_max = (long long)T * k < E ? (long long)T * k : E;
+  const int max_active = (int)routed_max + has_shared;
+  es::FfnArgs f{};
+  f.packed = static_cast<const uint8_t*>(packed);
+  f.expert_bytes = es::expert_bytes(cfg->hidden, cfg->inter);
+  f.D = cfg->hidden; f.I = cfg->inter;
+  f.n_active = w.n_active; f.act_e = w.act_e; f.act_off = w.act_off; f.act_n = w.act_n;
+  f.pair_tok = w.pair_tok; f.x_perm = w.x_perm; f.xsum = w.xsum;
+  f.h_hi = w.h_hi; f.h_lo = w.h_lo; f.y_pair = w.y_pair;
+  if (mk.mark(2, st) != cudaSuccess) return ES_ERR_CUDA;
+  if ((ce = es::launch_ffn_gateup(f, max_active, st)) != cudaSuccess) return ES_ERR_CUDA;
+  if (mk.mark(3, st) != cudaSuccess) return ES_ERR_CUDA;
+  if ((ce = es::launch_ffn_down(f, max_active, st)) != cudaSuccess) return ES_ERR_CUDA;
+  if (mk.mark(4, st) != cudaSuccess) return ES_ERR_CUDA;
+
+  es::CombineArgs cb{};
+  cb.idx = idx; cb.w = wts; cb.pos = w.pos; cb.sgate = w.sgate; cb.y_pair = w.y_pair;
+  cb.T = T; cb.D = cfg->hidden; cb.k = k; cb.has_shared = has_shared;
+  cb.out = out; cb.out_f32 = out_f32;
+  if (es::launch_combine(cb, st) != cudaSuccess) return ES_ERR_CUDA;
+  return cuda_status(mk.mark(5, st));
+}
+
+es_status check_common(const es_moe_cfg* cfg, const void* x, const void* packed,
+                       void* out, int32_t out_dtype, int32_t T, void* ws,
+                       size_t ws_bytes, Workspace* w) {
+  es_status s = check_cfg(cfg);
+  if (s != ES_OK) return s;
+  if (T < 0 || T > 65535) return ES_ERR_UNSUPPORTED;
+  if (out_dtype != ES_DTYPE_BF16 && out_dtype != ES_DTYPE_F32) return ES_ERR_UNSUPPORTED;
+  if (!ws || !aligned(ws, 256)) return ES_ERR_INVALID_ARG;
+  *w = es::carve_workspace(ws, cfg->hidden, cfg->num_experts, cfg->top_k, cfg->inter,
+                           cfg->shared_inter > 0, T);
+  if (ws_bytes < w->bytes) return ES_ERR_WORKSPACE;
+  if (T == 0) return ES_OK;
+  if (!x || !packed || !out) return ES_ERR_INVALID_ARG;
+  if (!aligned(x, 16) || !aligned(packed, 16) || !aligned(out, 16)) return ES_ERR_INVALID_ARG;
+  return ES_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* es_status_str(es_status status) {
+  switch (status) {
+    case ES_OK: return "ok";
+    case ES_ERR_INVALID_ARG: return "invalid argument";
+    case ES_ERR_UNSUPPORTED: return "unsupported shape";
+    case ES_ERR_WORKSPACE: return "workspace too small";
+    case ES_ERR_CUDA: return "CUDA runtime error";
+    case ES_ERR_DEVICE: return "device-side invariant violation";
+  }
+  return "unknown status";
+}
+
+int32_t es_version(void) { return (1 << 16) | 0; }
+
+es_status es_moe_packed_bytes(const es_moe_cfg* cfg, size_t* bytes_out) {
+  es_status s = check_cfg(cfg);
+  if (s != ES_OK) return s;
+  if (!bytes_out) return ES_ERR_INVALID_ARG;
+  const int E1 = cfg->num_experts + (cfg->shared_inter > 0 ? 1 : 0);
+  *bytes_out = es::expert_bytes(cfg->hidden, cfg->inter) * (size_t)E1;
+  return ES_OK;
+}
+
+es_status es_moe_prepare(const es_moe_cfg* cfg, const es_mlx_layer* layer,
+                         void* packed, size_t packed_bytes, es_stream_t stream) {
+  es_status s = check_cfg(cfg);
+  if (s != ES_OK) return s;
+  if (!layer || !packed || !aligned(packed, 256)) return ES_ERR_INVALID_ARG;
+  size_t need = 0;
+  es_moe_packed_bytes(cfg, &need);
+  if (packed_bytes < need) return ES_ERR_INVALID_ARG;
+  es::PrepareArgs a{};
+  const es_mlx_proj* routed[3] = {&layer->gate, &layer->up, &layer->down};
+  const es_mlx_proj* shared[3] = {&layer->shared_gate_proj, &layer->shared_up_proj,
+                                  &layer->shared_down_proj};
+  const int has_shared = cfg->shared_inter > 0;
+  for (int p = 0; p < 3; ++p) {
+    if (!routed[p]->weight || !routed[p]->scales || !routed[p]->biases) return ES_ERR_INVALID_ARG;
+    a.w[p] = routed[p]->weight; a.s[p] = routed[p]->scales; a.b[p] = routed[p]->biases;
+    if (has_shared) {
+      if (!shared[p]->weight || !shared[p]->scales || !shared[p]->biases) return ES_ERR_INVALID_ARG;
+      a.sw[p] = shared[p]->weight; a.ss[p] = shared[p]->scales; a.sb[p] = shared[p]->biases;
+    }
+  }
+  a.D = cfg->hidden; a.I = cfg->inter; a.E = cfg->num_experts; a.has_shared = has_shared;
+  a.packed = static_cast<uint8_t*>(packed);
+  return cuda_status(es::launch_prepare(a, static_cast<cudaStream_t>(stream)));
+}
+
+es_status es_moe_workspace_bytes(const es_moe_cfg* cfg, int32_t max_tokens, size_t* bytes_out) {
+  es_status s = check_cfg(cfg);
+  if (s != ES_OK) return s;
+  if (!bytes_out || max_tokens < 0 || max_tokens > 65535) return ES_ERR_INVALID_ARG;
+  *bytes_out = es::carve_workspace(nullptr, cfg->hidden, cfg->num_experts, cfg->top_k,
+                                   cfg->inter, cfg->shared_inter > 0, max_tokens).bytes;
+  return ES_OK;
+}
+
+es_status es_moe_route(const es_moe_cfg* cfg, const void* logits, int32_t logits_dtype,
+                       const float* cache_bias, int32_t T, int32_t* topk_idx, float* topk_w,
+                       es_stream_t stream) {
+  es_status s = check_cfg(cfg);
+  if (s != ES_OK) return s;
+  if (T < 0) return ES_ERR_INVALID_ARG;
+  if (logits_dtype != ES_DTYPE_BF16 && logits_dtype != ES_DTYPE_F32) return ES_ERR_UNSUPPORTED;
+  if (T == 0) return ES_OK;
+  if (!logits || !topk_idx || !topk_w) return ES_ERR_INVALID_ARG;
+  es::RouteArgs r{};
+  r.logits = logits; r.logits_f32 = logits_dtype == ES_DTYPE_F32; r.bias = cache_bias;
+  r.T = T; r.D = cfg->hidden; r.E = cfg->num_experts; r.k = cfg->top_k;
+  r.renorm = cfg->norm_topk_prob != 0; r.W = (T + 31) / 32;
+  r.out_idx = topk_idx; r.out_w = topk_w;
+  return cuda_status(es::launch_route(r, static_cast<cudaStream_t>(stream)));
+}
+
+es_status es_moe_expert_ffn(const es_moe_cfg* cfg, const void* x, const int32_t* topk_idx,
+                            const float* topk_w, const void* shared_gate_w, const void* packed,
+                            void* out, int32_t out_dtype, int32_t T, void* workspace,
+                            size_t workspace_bytes, es_stream_t stream) {
+  Workspace w{};
+  es_status s = check_common(cfg, x, packed, out, out_dtype, T, workspace, workspace_bytes, &w);
+  if (s != ES_OK || T == 0) return s;
+  if (!topk_idx || !topk_w) return ES_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(w.bitmap, 0, (size_t)w.E1 * w.W * 4, st) != cudaSuccess) return ES_ERR_CUDA;
+  es::RouteArgs r{};
+  r.in_idx = topk_idx; r.in_w = topk_w;
+  r.x = static_cast<const uint16_t*>(x);
+  r.sg_w = static_cast<const uint16_t*>(shared_gate_w);
+  r.T = T; r.D = cfg->hidden; r.E = cfg->num_experts; r.k = cfg->top_k;
+  r.renorm = cfg->norm_topk_prob != 0; r.has_shared = cfg->shared_inter > 0; r.W = w.W;
+  r.bitmap = w.bitmap; r.sgate = w.sgate; r.x_perm = w.x_perm; r.xsum = w.xsum; r.err = w.err;
+  if (es::launch_route(r, st) != cudaSuccess) return ES_ERR_CUDA;
+  return run_ffn(cfg, w, topk_idx, topk_w, packed, out, out_dtype == ES_DTYPE_F32, T, st);
+}
+
+es_status es_moe_forward(const es_moe_cfg* cfg, const void* x, const void* logits,
+                         int32_t logits_dtype, const float* cache_bias, const void* shared_gate_w,
+                         const void* packed, void* out, int32_t out_dtype, int32_t* topk_idx,
+                         float* topk_w, int32_t T, void* workspace, size_t workspace_bytes,
+                         es_stream_t stream) {
+  return es_moe_forward_timed(cfg, x, logits, logits_dtype, cache_bias, shared_gate_w, packed, out,
+                              out_dtype, topk_idx, topk_w, T, workspace, workspace_bytes, stream,
+                              nullptr, 0);
+}
+
+es_status es_moe_forward_timed(const es_moe_cfg* cfg, const void* x, const void* logits,
+                               int32_t logits_dtype, const float* cache_bias,
+                               const void* shared_gate_w, const void* packed, void* out,
+                               int32_t out_dtype, int32_t* topk_idx, float* topk_w, int32_t T,
+                               void* workspace, size_t workspace_bytes, es_stream_t stream,
+                               void* const* events, int32_t n_events) {
+  Workspace w{};
+  es_status s = check_common(cfg, x, packed, out, out_dtype, T, workspace, workspace_bytes, &w);
+  if (s != ES_OK || T == 0) return s;
+  if (!logits) return ES_ERR_INVALID_ARG;
+  if (logits_dtype != ES_DTYPE_BF16 && logits_dtype != ES_DTYPE_F32) return ES_ERR_UNSUPPORTED;
+  if (events && n_events != 6) return ES_ERR_INVALID_ARG;
+  Marks mk;
+  mk.ev = events;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t* idx = topk_idx ? topk_idx : w.topk_idx;
+  float* wts = topk_w ? topk_w : w.topk_w;
+  if (cudaMemsetAsync(w.bitmap, 0, (size_t)w.E1 * w.W * 4, st) != cudaSuccess) return ES_ERR_CUDA;
+  es::RouteArgs r{};
+  r.logits = logits; r.logits_f32 = logits_dtype == ES_DTYPE_F32; r.bias = cache_bias;
+  r.x = static_cast<const uint16_t*>(x);
+  r.sg_w = static_cast<const uint16_t*>(shared_gate_w);
+  r.T = T; r.D = cfg->hidden; r.E = cfg->num_experts; r.k = cfg->top_k;
+  r.renorm = cfg->norm_topk_prob != 0; r.has_shared = cfg->shared_inter > 0; r.W = w.W;
+  r.out_idx = idx; r.out_w = wts;
+  r.bitmap = w.bitmap; r.sgate = w.sgate; r.x_perm = w.x_perm; r.xsum = w.xsum; r.err = w.err;
+  if (mk.mark(0, st) != cudaSuccess) return ES_ERR_CUDA;
+  if (es::launch_route(r, st) != cudaSuccess) return ES_ERR_CUDA;
+  return run_ffn(cfg, w, idx, wts, packed, out, out_dtype == ES_DTYPE_F32, T, st, mk);
+}
+
+es_status es_moe_read_error(const void* workspace, int32_t clear, uint32_t* flags_out,
+                            es_stream_t stream) {
+  if (!workspace || !flags_out || !aligned(workspace, 256)) return ES_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t v = 0;
+  if (cudaMemcpyAsync(&v, workspace, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) return ES_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return ES_ERR_CUDA;
+  if (clear && cudaMemsetAsync(const_cast<void*>(workspace), 0, 4, st) != cudaSuccess)
+    return ES_ERR_CUDA;
+  *flags_out = v;
+  return ES_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,92 @@
+// Launch arguments and host launchers of the MoE block kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "es_layout.h"
+
+namespace es {
+
+struct RouteArgs {
+  // routing source: either logits (+ optional bias) or given top-k
+  const void* logits;       // [T][E] bf16 or f32
+  int logits_f32;
+  const float* bias;        // [E] or null
+  const int32_t* in_idx;    // [T][k] given routing, or null
+  const float* in_w;        // [T][k]
+  // activations
+  const uint16_t* x;        // [T][D] bf16 or null (route only)
+  const uint16_t* sg_w;     // [D] bf16 shared gate weight or null
+  int T, D, E, k, renorm, has_shared, W;
+  // outputs
+  int32_t* out_idx;         // [T][k] or null
+  float* out_w;             // [T][k] or null
+  uint32_t* bitmap;         // [E1][W] or null
+  float* sgate;             // [T] or null
+  uint16_t* x_perm;         // [T][D] or null
+  float* xsum;              // [T][D/64] or null
+  uint32_t* err;
+};
+
+struct DispatchArgs {
+  const uint32_t* bitmap;
+  const int32_t* idx;       // [T][k]
+  int T, E, k, has_shared, W;
+  int32_t* wpre;
+  int32_t* n_active;
+  int32_t* act_e;
+  int32_t* act_off;
+  int32_t* act_n;
+  int32_t* pair_tok;
+  int32_t* pos;             // [T][kk]
+};
+
+struct FfnArgs {
+  const uint8_t* packed;
+  size_t expert_bytes;
+  int D, I;
+  const int32_t* n_active;
+  const int32_t* act_e;
+  const int32_t* act_off;
+  const int32_t* act_n;
+  const int32_t* pair_tok;
+  const uint16_t* x_perm;
+  const float* xsum;
+  uint16_t* h_hi;
+  uint16_t* h_lo;
+  float* y_pair;
+};
+
+struct CombineArgs {
+  const int32_t* idx;       // [T][k]
+  const float* w;           // [T][k]
+  const int32_t* pos;       // [T][kk]
+  const float* sgate;       // [T]
+  const float* y_pair;      // [P][D]
+  int T, D, k, has_shared;
+  void* out;
+  int out_f32;
+};
+
+struct PrepareArgs {
+  // routed experts, stacked [E, N, K/8] / [E, N, K/64]
+  const uint32_t* w[3];
+  const uint16_t* s[3];
+  const uint16_t* b[3];
+  // shared expert (no expert axis) or nulls
+  const uint32_t* sw[3];
+  const uint16_t* ss[3];
+  const uint16_t* sb[3];
+  int D, I, E, has_shared;
+  uint8_t* packed;
+};
+
+cudaError_t launch_route(const RouteArgs& a, cudaStream_t st);
+cudaError_t launch_dispatch(const DispatchArgs& a, cudaStream_t st);
+cudaError_t launch_ffn_gateup(const FfnArgs& a, int max_active, cudaStream_t st);
+cudaError_t launch_ffn_down(const FfnArgs& a, int max_active, cudaStream_t st);
+cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);
+cudaError_t launch_prepare(const PrepareArgs& a, cudaStream_t st);
+
+}  // namespace es

@@ -1,0 +1,146 @@
+// Packed weight layout and workspace layout of the MoE block. Shared by host
+// and device code.
+//
+// Packed layout (one layer, built once by es_moe_prepare):
+//   experts 0..E-1 (then the shared expert, if any), each exactly
+//   3*D*I*9/16 bytes -- the reference's per-expert bytes, no padding.
+//   Inside an expert:
+//     gate/up region: for rb in [0, I/16), G in [0, D/64), proj in {gate, up}:
+//                     one 576-byte tile
+//     down region:    for rb in [0, D/16), G in [0, I/64): one 576-byte tile
+//   A tile covers 16 rows x 64 columns (one quantisation group):
+//     bytes [0, 512)  codes. Lane l = 4*g + c of a warp owns bytes
+//                     [16l, 16l + 16): words 2c and 2c+1 of the group for
+//                     row g, then the same two words for row g + 8 -- the
+//                     exact A fragment of four m16n8k16 steps.
+//     bytes [512, 576) for g in 0..7: (scale, bias) of row g then of row
+//                     g + 8, fp16 each -- 8 bytes per g.
+//   Column k of a tile row is nibble k % 8 of word k / 8, as in MLX.
+//
+// Activation operand layout ("fragment order"), used for x and h: a row of
+// K values is stored as K/16 chunks of 16; chunk q holds, for s in 0..3 and
+// slot in 0..3, element 16q + s + 4*slot at position 4s + slot. A lane that
+// reads chunk q of a group gets its two B-fragment registers for each of the
+// four k-steps as consecutive words.
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifndef __CUDACC__
+#define __host__
+#define __device__
+#endif
+
+namespace es {
+
+constexpr int kGroup = 64;
+constexpr int kTileBytes = 576;
+constexpr int kTileCodeBytes = 512;
+constexpr int kMaxTopK = 16;
+constexpr int kMaxExperts = 1024;
+
+__host__ __device__ inline size_t expert_bytes(int D, int I) {
+  return (size_t)3 * D * I * 9 / 16;
+}
+__host__ __device__ inline size_t gateup_region_bytes(int D, int I) {
+  return (size_t)2 * D * I * 9 / 16;
+}
+__host__ __device__ inline size_t gateup_tile_off(int GD, int rb, int G, int proj) {
+  return ((size_t)(rb * GD + G) * 2 + proj) * kTileBytes;
+}
+__host__ __device__ inline size_t down_tile_off(int D, int I, int rb, int G) {
+  return gateup_region_bytes(D, I) + (size_t)(rb * (I / kGroup) + G) * kTileBytes;
+}
+// position of element d (0..K-1) of a row in fragment order
+__host__ __device__ inline int frag_pos(int d) {
+  const int q = d >> 4, r = d & 15;
+  return (q << 4) + 4 * (r & 3) + (r >> 2);
+}
+
+inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// Device pointers carved from the caller's workspace for a call with T tokens.
+struct Workspace {
+  uint32_t* err;       // [64] error word + reserved
+  uint32_t* bitmap;    // [E1][W]   token bitmap per expert
+  int32_t* wpre;       // [E1][W]   exclusive popcount prefix per word
+  int32_t* n_active;   // [1]
+  int32_t* act_e;      // [E1]      active expert ids, ascending
+  int32_t* act_off;    // [E1]      first sorted pair of each active expert
+  int32_t* act_n;      // [E1]      pairs of each active expert
+  int32_t* pair_tok;   // [P]       token of each sorted pair
+  int32_t* pos;        // [T][kk]   sorted pair of (token, slot), -1 = none
+  int32_t* topk_idx;   // [T][k]
+  float* topk_w;       // [T][k]
+  float* sgate;        // [T]       shared-expert gate
+  uint16_t* x_perm;    // [T][D]    bf16, fragment order
+  float* xsum;         // [T][D/64]
+  uint16_t* h_hi;      // [P][I]    bf16 high part of h, fragment order
+  uint16_t* h_lo;      // [P][I]    bf16 remainder h - hi
+  float* y_pair;       // [P][D]
+  int W, P, kk, E1;
+  size_t bytes;
+};
+
+// Carve (or, with base == nullptr, just size) the workspace for T tokens.
+inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
+                                 int has_shared, int T) {
+  Workspace w{};
+  const int E1 = E + (has_shared ? 1 : 0);
+  const int W = (T + 31) / 32 > 0 ? (T + 31) / 32 : 1;
+  const int kk = k + (has_shared ? 1 : 0);
+  const int P = (T > 0 ? T : 1) * kk;
+  const int Tm = T > 0 ? T : 1;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  size_t o_err = take(256);
+  size_t o_bitmap = take((size_t)E1 * W * 4);
+  size_t o_wpre = take((size_t)E1 * W * 4);
+  size_t o_nact = take(4);
+  size_t o_acte = take((size_t)E1 * 4);
+  size_t o_actoff = take((size_t)E1 * 4);
+  size_t o_actn = take((size_t)E1 * 4);
+  size_t o_ptok = take((size_t)P * 4);
+  size_t o_pos = take((size_t)Tm * kk * 4);
+  size_t o_tidx = take((size_t)Tm * k * 4);
+  size_t o_tw = take((size_t)Tm * k * 4);
+  size_t o_sg = take((size_t)Tm * 4);
+  size_t o_xp = take((size_t)Tm * D * 2);
+  size_t o_xs = take((size_t)Tm * (D / kGroup) * 4);
+  size_t o_hh = take((size_t)P * I * 2);
+  size_t o_hl = take((size_t)P * I * 2);
+  size_t o_y = take((size_t)P * D * 4);
+  w.bytes = off;
+  w.W = W;
+  w.P = P;
+  w.kk = kk;
+  w.E1 = E1;
+  if (base) {
+    char* b = static_cast<char*>(base);
+    w.err = reinterpret_cast<uint32_t*>(b + o_err);
+    w.bitmap = reinterpret_cast<uint32_t*>(b + o_bitmap);
+    w.wpre = reinterpret_cast<int32_t*>(b + o_wpre);
+    w.n_active = reinterpret_cast<int32_t*>(b + o_nact);
+    w.act_e = reinterpret_cast<int32_t*>(b + o_acte);
+    w.act_off = reinterpret_cast<int32_t*>(b + o_actoff);
+    w.act_n = reinterpret_cast<int32_t*>(b + o_actn);
+    w.pair_tok = reinterpret_cast<int32_t*>(b + o_ptok);
+    w.pos = reinterpret_cast<int32_t*>(b + o_pos);
+    w.topk_idx = reinterpret_cast<int32_t*>(b + o_tidx);
+    w.topk_w = reinterpret_cast<float*>(b + o_tw);
+    w.sgate = reinterpret_cast<float*>(b + o_sg);
+    w.x_perm = reinterpret_cast<uint16_t*>(b + o_xp);
+    w.xsum = reinterpret_cast<float*>(b + o_xs);
+    w.h_hi = reinterpret_cast<uint16_t*>(b + o_hh);
+    w.h_lo = reinterpret_cast<uint16_t*>(b + o_hl);
+    w.y_pair = reinterpret_cast<float*>(b + o_y);
+  }
+  return w;
+}
+
+}  // namespace es

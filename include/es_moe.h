@@ -1,0 +1,192 @@
+/*
+ * es_moe.h — C ABI of the B200 MoE block (router -> dispatch -> 4-bit expert
+ * FFN -> combine) for Expert Sniper's MLX-affine expert format.
+ *
+ * Conventions
+ *   - Every pointer argument except `cfg` and the `*_bytes` / error outputs is
+ *     caller-owned DEVICE memory on the current CUDA device.
+ *   - Nothing here allocates device memory, and nothing on the forward path
+ *     synchronises the host: kernels are queued on `stream` (a cudaStream_t
+ *     passed as void*, NULL = legacy default stream).
+ *   - Errors are status codes; no exception crosses this boundary. Invariant
+ *     violations detected inside a kernel are recorded in an error word that
+ *     lives in the workspace and is read with es_moe_read_error().
+ *   - Calls that share a workspace must be ordered on one stream.
+ *
+ * Expert weight format (the reference's on-disk / MLX format, one expert):
+ *   gate_proj / up_proj : weight [I, D/8] uint32, scales [I, D/64] fp16,
+ *                         biases [I, D/64] fp16
+ *   down_proj           : weight [D, I/8] uint32, scales [D, I/64] fp16,
+ *                         biases [D, I/64] fp16
+ *   code q of column k sits in bits 4*(k%8) of word k/8 of its row, and
+ *   w = scale * q + bias per 64-column group.
+ * (src/mlx_expert_sniper/download.py:73-77 TENSOR_ORDER, download.py:189-248,
+ *  src/mlx_expert_sniper/engine.py:12-13 BITS=4, GROUP_SIZE=64.)
+ */
+#ifndef ES_MOE_H
+#define ES_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(ES_BUILD_LIB) && defined(__GNUC__)
+#define ES_API __attribute__((visibility("default")))
+#else
+#define ES_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* es_stream_t; /* cudaStream_t */
+
+typedef enum es_status {
+  ES_OK = 0,
+  ES_ERR_INVALID_ARG = 1,   /* null pointer, bad size, misaligned buffer     */
+  ES_ERR_UNSUPPORTED = 2,   /* shape outside what the kernels implement      */
+  ES_ERR_WORKSPACE = 3,     /* workspace smaller than es_moe_workspace_bytes */
+  ES_ERR_CUDA = 4,          /* a CUDA runtime call failed                    */
+  ES_ERR_DEVICE = 5         /* a kernel flagged an invariant violation       */
+} es_status;
+
+typedef enum es_dtype {
+  ES_DTYPE_BF16 = 0,
+  ES_DTYPE_F16 = 1,
+  ES_DTYPE_F32 = 2
+} es_dtype;
+
+/* Device error word bits (es_moe_read_error). */
+#define ES_DEVERR_BAD_EXPERT_ID 0x1u   /* top-k index outside [-1, E)        */
+#define ES_DEVERR_NONFINITE_LOGIT 0x2u /* NaN logit seen by the router        */
+#define ES_DEVERR_CAPACITY 0x4u        /* pair list larger than the workspace */
+
+/* Shape of one MoE block. Mirrors the streaming config.json keys the
+ * reference reads (download.py:477-523: num_experts, num_experts_per_tok,
+ * moe_intermediate_size, norm_topk_prob, shared_expert_intermediate_size,
+ * quantization{bits, group_size}). */
+typedef struct es_moe_cfg {
+  int32_t hidden;         /* D, multiple of 256, <= 4096                       */
+  int32_t num_experts;    /* E routed experts, 1..1024                       */
+  int32_t top_k;          /* k, 1..16, k <= E                                 */
+  int32_t inter;          /* I: 256, 512, 768, 1024, 1536 or 2048             */
+  int32_t group_size;     /* must be 64                                       */
+  int32_t bits;           /* must be 4                                        */
+  int32_t norm_topk_prob; /* 1: renormalise the k selected probabilities      */
+  int32_t shared_inter;   /* 0: no shared expert; else its I (must == inter)  */
+} es_moe_cfg;
+
+/* Per-projection MLX tensors for all experts of one layer, stacked on a
+ * leading expert axis ([E, ...]), device pointers. The shared expert, when
+ * cfg->shared_inter > 0, is passed separately without the expert axis. */
+typedef struct es_mlx_proj {
+  const uint32_t* weight; /* [E, N, K/8]  */
+  const uint16_t* scales; /* [E, N, K/64] fp16 bits */
+  const uint16_t* biases; /* [E, N, K/64] fp16 bits */
+} es_mlx_proj;
+
+typedef struct es_mlx_layer {
+  es_mlx_proj gate; /* N = I, K = D */
+  es_mlx_proj up;   /* N = I, K = D */
+  es_mlx_proj down; /* N = D, K = I */
+  es_mlx_proj shared_gate_proj; /* shared expert, no expert axis, or NULLs */
+  es_mlx_proj shared_up_proj;
+  es_mlx_proj shared_down_proj;
+} es_mlx_layer;
+
+/* Static string for a status code. */
+ES_API const char* es_status_str(es_status status);
+
+/* ABI version, (major << 16) | minor. */
+ES_API int32_t es_version(void);
+
+/* Bytes of the packed (device-resident) weights of one layer: exactly the
+ * reference's per-expert bytes 3*D*I*0.5625 times (E + has_shared).
+ * Replaces the per-call re-stacking of `stack_proj`
+ * (src/mlx_expert_sniper/engine.py:22-30): the layout is built once. */
+ES_API es_status es_moe_packed_bytes(const es_moe_cfg* cfg, size_t* bytes_out);
+
+/* One-time repack of a layer's MLX tensors into the tiled device layout the
+ * kernels stream. `packed` must be 256-byte aligned and hold
+ * es_moe_packed_bytes() bytes. Counterpart of reader.get_experts + stack_proj
+ * (src/mlx_expert_sniper/expert_io.py:420-436, engine.py:22-30). */
+ES_API es_status es_moe_prepare(const es_moe_cfg* cfg, const es_mlx_layer* layer,
+                         void* packed, size_t packed_bytes, es_stream_t stream);
+
+/* Workspace bytes needed by es_moe_forward / es_moe_expert_ffn for up to
+ * `max_tokens` tokens per call. */
+ES_API es_status es_moe_workspace_bytes(const es_moe_cfg* cfg, int32_t max_tokens,
+                                 size_t* bytes_out);
+
+/* Router: logits (+ optional additive cache bias, promoted to fp32) ->
+ * softmax (fp32) -> top-k -> optional renormalisation.
+ *   logits     [T, E] bf16 or f32 (logits_dtype)
+ *   cache_bias [E] f32 or NULL (NULL = no bias, as for bias == 0)
+ *   topk_idx   [T, k] int32 out, in descending probability order
+ *   topk_w     [T, k] f32 out
+ * Ties in the selection key go to the lower expert id.
+ * Counterpart of src/mlx_expert_sniper/generate.py:122-136 (and
+ * engine_30b.py:158-165, models/qwen4_exp.py:463-472). */
+ES_API es_status es_moe_route(const es_moe_cfg* cfg, const void* logits,
+                       int32_t logits_dtype, const float* cache_bias,
+                       int32_t T, int32_t* topk_idx, float* topk_w,
+                       es_stream_t stream);
+
+/* Expert FFN + combine for given routing:
+ *   out[t] = sum_j w[t,j] * down(silu(gate(x_t)) * up(x_t))[idx[t,j]]
+ *            (+ sigmoid(x_t . shared_gate_w) * shared(x_t) if shared)
+ * An index of -1 skips that slot (the partition mask of the expert-parallel
+ * partial). The k terms of a token are summed in ascending expert id order,
+ * in fp32; the shared term is added last.
+ *   x              [T, D] bf16
+ *   topk_idx       [T, k] int32 in [-1, E)
+ *   topk_w         [T, k] f32
+ *   shared_gate_w  [D] bf16 or NULL (NULL with a shared expert = gate 1.0)
+ *   out            [T, D] bf16 or f32 (out_dtype)
+ * Counterpart of run_expert_ffn (src/mlx_expert_sniper/engine.py:15-42,
+ * engine_30b.py:15-42, engine_next.py:15-42), the shared expert of
+ * generate.py:173-178, and compute_partial's masking
+ * (src/expert_network/node.py:142-172). */
+ES_API es_status es_moe_expert_ffn(const es_moe_cfg* cfg, const void* x,
+                            const int32_t* topk_idx, const float* topk_w,
+                            const void* shared_gate_w, const void* packed,
+                            void* out, int32_t out_dtype, int32_t T,
+                            void* workspace, size_t workspace_bytes,
+                            es_stream_t stream);
+
+/* The whole block: es_moe_route followed by es_moe_expert_ffn, sharing the
+ * workspace. topk_idx / topk_w may be NULL (kept in the workspace).
+ * Counterpart of the MoE part of make_forward's layer loop
+ * (src/mlx_expert_sniper/generate.py:122-181). */
+ES_API es_status es_moe_forward(const es_moe_cfg* cfg, const void* x,
+                         const void* logits, int32_t logits_dtype,
+                         const float* cache_bias, const void* shared_gate_w,
+                         const void* packed, void* out, int32_t out_dtype,
+                         int32_t* topk_idx, float* topk_w, int32_t T,
+                         void* workspace, size_t workspace_bytes,
+                         es_stream_t stream);
+
+/* es_moe_forward with instrumentation: `events` holds 6 cudaEvent_t that are
+ * recorded on `stream` before the router, dispatch, gate/up, down and combine
+ * kernels and after the combine, so the caller can read each kernel's device
+ * time with cudaEventElapsedTime. n_events must be 6 (or events NULL). */
+ES_API es_status es_moe_forward_timed(const es_moe_cfg* cfg, const void* x,
+                                      const void* logits, int32_t logits_dtype,
+                                      const float* cache_bias,
+                                      const void* shared_gate_w, const void* packed,
+                                      void* out, int32_t out_dtype,
+                                      int32_t* topk_idx, float* topk_w, int32_t T,
+                                      void* workspace, size_t workspace_bytes,
+                                      es_stream_t stream, void* const* events,
+                                      int32_t n_events);
+
+/* Synchronously read (and clear when `clear` != 0) the device error word of
+ * a workspace. Blocks the host on `stream`. */
+ES_API es_status es_moe_read_error(const void* workspace, int32_t clear,
+                            uint32_t* flags_out, es_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ES_MOE_H */

@@ -1,0 +1,100 @@
+"""The C ABI library on the host: it loads, exports every declared entry
+point, and its host-only entry points (sizes, argument checks) behave,
+without touching a GPU."""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import pytest
+
+from expert_sniper_b200 import PRESETS, MoEConfig, _native
+from expert_sniper_b200.config import CMoECfg
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(_native.LIB_PATH):
+        from expert_sniper_b200 import build
+        build.build()
+    return _native.lib()
+
+
+def test_exports_every_header_function(lib):
+    names = _native.header_functions()
+    assert len(names) >= 9
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in es_moe.h but not exported"
+    # and nothing else is exported under the es_ prefix
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", _native.LIB_PATH], capture_output=True,
+                         text=True).stdout
+    exported = sorted({line.split()[-1] for line in out.splitlines()
+                       if line.split()[-1].startswith("es_")})
+    assert exported == names
+
+
+def test_signature_table_covers_header():
+    assert sorted(_native._SIGNATURES) == _native.header_functions()
+
+
+def test_version_and_status_strings(lib):
+    assert lib.es_version() >> 16 == 1
+    assert lib.es_status_str(0) == b"ok"
+    assert lib.es_status_str(3) == b"workspace too small"
+    assert lib.es_status_str(99) == b"unknown status"
+
+
+@pytest.mark.parametrize("name", sorted(PRESETS))
+def test_packed_bytes_equal_reference_block_bytes(lib, name):
+    cfg = PRESETS[name]
+    nb = _native.packed_bytes(cfg.to_c())
+    assert nb == cfg.packed_bytes
+    # the reference's per-expert block bytes (SURVEY byte table / download.py)
+    per = {"olmoe-1b-7b": 3538944, "qwen3-30b-a3b": 2654208, "qwen3-next-80b-a3b": 1769472,
+           "qwen3-235b-a22b": 10616832}[name]
+    assert cfg.bytes_per_expert == per
+
+
+def test_workspace_bytes_monotone(lib):
+    c = PRESETS["qwen3-30b-a3b"].to_c()
+    sizes = [_native.workspace_bytes(c, t) for t in (0, 1, 8, 64, 256, 4096)]
+    assert sizes == sorted(sizes) and sizes[1] > 0
+
+
+@pytest.mark.parametrize("bad", [
+    dict(group_size=32), dict(bits=8), dict(hidden=2000), dict(hidden=8192), dict(inter=640),
+    dict(num_experts=2000), dict(top_k=17), dict(top_k=0), dict(shared_inter=256),
+])
+def test_unsupported_configs_rejected(lib, bad):
+    base = dict(hidden=2048, num_experts=128, top_k=8, inter=768, group_size=64, bits=4,
+                norm_topk_prob=1, shared_inter=0)
+    base.update(bad)
+    c = CMoECfg(**base)
+    out = ctypes.c_size_t(0)
+    st = lib.es_moe_packed_bytes(ctypes.byref(c), ctypes.byref(out))
+    assert st in (1, 2)
+
+
+def test_null_and_size_checks_return_status(lib):
+    c = PRESETS["qwen3-30b-a3b"].to_c()
+    assert lib.es_moe_packed_bytes(None, None) == 1
+    assert lib.es_moe_workspace_bytes(ctypes.byref(c), -1, ctypes.byref(ctypes.c_size_t())) == 1
+    # workspace too small is reported before any launch
+    st = lib.es_moe_forward(ctypes.byref(c), 16, 16, 0, None, None, 256, 256, 0, None, None, 4,
+                            256, 1, None)
+    assert st == 3
+    # T == 0 is a no-op success
+    assert lib.es_moe_route(ctypes.byref(c), None, 0, None, 0, None, None, None) == 0
+    # misaligned workspace
+    assert lib.es_moe_expert_ffn(ctypes.byref(c), 16, 16, 16, None, 256, 256, 0, 1, 8, 1 << 30,
+                                 None) == 1
+    # read_error validates before touching the device
+    assert lib.es_moe_read_error(None, 0, None, None) == 1
+
+
+def test_config_validation_in_python():
+    with pytest.raises(ValueError):
+        MoEConfig(2048, 128, 8, 768, True, shared_inter=512)
+    with pytest.raises(ValueError):
+        MoEConfig(2048, 4, 8, 768, True)
