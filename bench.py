@@ -205,7 +205,8 @@ def run_ours_single(args):
     setup_s = time.time() - t_setup
     bias = cache_bias_vector(cfg.num_experts, 0.5, 0)[0].to(dev)
     Tmax = max([T] + sweep)
-    blocks = [MoEBlock(cfg, packed=p, max_tokens=Tmax) for p in packed]
+    ws = MoEBlock.new_workspace(cfg, Tmax, dev)  # layers run in sequence: one workspace
+    blocks = [MoEBlock(cfg, packed=p, max_tokens=Tmax, workspace=ws) for p in packed]
     stream = torch.cuda.Stream(dev)
     peak, peak_kind = measured_peaks()
 

@@ -86,7 +86,8 @@ class MoEBlock:
     """
 
     def __init__(self, cfg: MoEConfig, weights: dict = None, packed: torch.Tensor = None,
-                 shared_gate_w: torch.Tensor = None, max_tokens: int = 64):
+                 shared_gate_w: torch.Tensor = None, max_tokens: int = 64,
+                 workspace: torch.Tensor = None):
         if (weights is None) == (packed is None):
             raise ValueError("pass exactly one of weights= or packed=")
         self.cfg = cfg
@@ -101,15 +102,29 @@ class MoEBlock:
             self.shared_gate_w = shared_gate_w.to(self.device, torch.bfloat16).contiguous()
         self._ws = None
         self._ws_tokens = -1
-        self.reserve(max_tokens)
+        if workspace is not None:
+            # a workspace shared by blocks that run one after another on one stream
+            if workspace.numel() < _native.workspace_bytes(self.ccfg, max_tokens):
+                raise ValueError("workspace smaller than es_moe_workspace_bytes(max_tokens)")
+            self._ws = workspace
+            self._ws_tokens = max_tokens
+        else:
+            self.reserve(max_tokens)
 
     # -- workspace --------------------------------------------------------
     def reserve(self, max_tokens: int) -> None:
+        """Grow the workspace to `max_tokens` tokens (zero-filled, as the
+        C ABI requires before first use)."""
         if max_tokens <= self._ws_tokens:
             return
         nb = _native.workspace_bytes(self.ccfg, max_tokens)
         self._ws = torch.zeros(nb, dtype=torch.uint8, device=self.device)
         self._ws_tokens = max_tokens
+
+    @staticmethod
+    def new_workspace(cfg: MoEConfig, max_tokens: int, device="cuda") -> torch.Tensor:
+        nb = _native.workspace_bytes(cfg.to_c(), max_tokens)
+        return torch.zeros(nb, dtype=torch.uint8, device=device)
 
     @property
     def workspace(self) -> torch.Tensor:

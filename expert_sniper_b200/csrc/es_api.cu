@@ -16,7 +16,10 @@ es_status check_cfg(const es_moe_cfg* c) {
   if (c->hidden <= 0 || c->inter <= 0 || c->num_experts <= 0 || c->top_k <= 0)
     return ES_ERR_INVALID_ARG;
   // gate/up CTAs give each warp 4 groups of D; down warps hold I/64 tiles
-  if (c->hidden % 256 || c->hidden > 4096) return ES_ERR_UNSUPPORTED;
+  const int nw = c->hidden / 256;
+  if (c->hidden % 256 || !(nw == 1 || nw == 2 || nw == 3 || nw == 4 || nw == 6 || nw == 8 ||
+                           nw == 12 || nw == 16))
+    return ES_ERR_UNSUPPORTED;
   const int kg = c->inter / 64;
   if (c->inter % 64 || !(kg == 4 || kg == 8 || kg == 12 || kg == 16 || kg == 24 || kg == 32))
     return ES_ERR_UNSUPPORTED;
@@ -47,21 +50,33 @@ struct Marks {
   }
 };
 
-// Shared tail of es_moe_forward / es_moe_expert_ffn: dispatch, FFN, combine.
-es_status run_ffn(const es_moe_cfg* cfg, const Workspace& w, const int32_t* idx,
-                  const float* wts, const void* packed, void* out, int out_f32,
-                  int T, cudaStream_t st, const Marks& mk = Marks()) {
+es::DispatchArgs dispatch_args(const es_moe_cfg* cfg, const Workspace& w, const int32_t* idx,
+                               const float* wts, int T) {
+  es::DispatchArgs d{};
+  d.bitmap = w.bitmap; d.idx = idx; d.w = wts; d.T = T; d.E = cfg->num_experts; d.k = cfg->top_k;
+  d.has_shared = cfg->shared_inter > 0; d.W = w.W; d.wpre = w.wpre; d.n_active = w.n_active;
+  d.act_e = w.act_e; d.act_off = w.act_off; d.act_n = w.act_n;
+  d.pair_tok = w.pair_tok; d.pos_shared = w.pos; d.cs_pos = w.cs_pos; d.cs_w = w.cs_w;
+  d.ticket = w.ticket; d.item_ctr = w.item_ctr;
+  return d;
+}
+
+// Front end: router (or given routing), operand prep and dispatch, one launch.
+es_status run_front(const es_moe_cfg* cfg, const Workspace& w, es::RouteArgs r,
+                    const int32_t* idx, const float* wts, int T, cudaStream_t st,
+                    const Marks& mk) {
+  es::DispatchArgs d = dispatch_args(cfg, w, idx, wts, T);
+  r.bitmap = w.bitmap;
+  if (mk.mark(0, st) != cudaSuccess) return ES_ERR_CUDA;
+  if (es::launch_front(r, d, st) != cudaSuccess) return ES_ERR_CUDA;
+  return cuda_status(mk.mark(1, st));
+}
+
+// Shared tail of es_moe_forward / es_moe_expert_ffn: FFN and combine.
+es_status run_ffn(const es_moe_cfg* cfg, const Workspace& w, const void* packed, void* out,
+                  int out_f32, int T, cudaStream_t st, const Marks& mk) {
   const int E = cfg->num_experts, k = cfg->top_k;
   const int has_shared = cfg->shared_inter > 0;
-  es::DispatchArgs d{};
-  d.bitmap = w.bitmap; d.idx = idx; d.T = T; d.E = E; d.k = k;
-  d.has_shared = has_shared; d.W = w.W; d.wpre = w.wpre; d.n_active = w.n_active;
-  d.act_e = w.act_e; d.act_off = w.act_off; d.act_n = w.act_n;
-  d.pair_tok = w.pair_tok; d.pos = w.pos;
-  if (mk.mark(1, st) != cudaSuccess) return ES_ERR_CUDA;
-  cudaError_t ce = es::launch_dispatch(d, st);
-  if (ce != cudaSuccess) return ES_ERR_CUDA;
-
   const long long routed_max = (long long)T * k < E ? (long long)T * k : E;
   const int max_active = (int)routed_max + has_shared;
   es::FfnArgs f{};
@@ -70,15 +85,16 @@ es_status run_ffn(const es_moe_cfg* cfg, const Workspace& w, const int32_t* idx,
   f.D = cfg->hidden; f.I = cfg->inter;
   f.n_active = w.n_active; f.act_e = w.act_e; f.act_off = w.act_off; f.act_n = w.act_n;
   f.pair_tok = w.pair_tok; f.x_perm = w.x_perm; f.xsum = w.xsum;
-  f.h_hi = w.h_hi; f.h_lo = w.h_lo; f.y_pair = w.y_pair;
+  f.h16 = w.h16; f.y_pair = w.y_pair; f.err = w.err;
+  f.partials = w.partials; f.counters = w.counters; f.item_ctr = w.item_ctr;
+  f.split_k = es::ffn_split_k(T, max_active, cfg->hidden, cfg->inter);
   if (mk.mark(2, st) != cudaSuccess) return ES_ERR_CUDA;
-  if ((ce = es::launch_ffn_gateup(f, max_active, st)) != cudaSuccess) return ES_ERR_CUDA;
+  if (es::launch_ffn_gateup(f, max_active, st) != cudaSuccess) return ES_ERR_CUDA;
   if (mk.mark(3, st) != cudaSuccess) return ES_ERR_CUDA;
-  if ((ce = es::launch_ffn_down(f, max_active, st)) != cudaSuccess) return ES_ERR_CUDA;
+  if (es::launch_ffn_down(f, max_active, st) != cudaSuccess) return ES_ERR_CUDA;
   if (mk.mark(4, st) != cudaSuccess) return ES_ERR_CUDA;
-
   es::CombineArgs cb{};
-  cb.idx = idx; cb.w = wts; cb.pos = w.pos; cb.sgate = w.sgate; cb.y_pair = w.y_pair;
+  cb.cs_pos = w.cs_pos; cb.cs_w = w.cs_w; cb.pos_shared = w.pos; cb.sgate = w.sgate; cb.y_pair = w.y_pair;
   cb.T = T; cb.D = cfg->hidden; cb.k = k; cb.has_shared = has_shared;
   cb.out = out; cb.out_f32 = out_f32;
   if (es::launch_combine(cb, st) != cudaSuccess) return ES_ERR_CUDA;
@@ -178,7 +194,8 @@ es_status es_moe_route(const es_moe_cfg* cfg, const void* logits, int32_t logits
   r.T = T; r.D = cfg->hidden; r.E = cfg->num_experts; r.k = cfg->top_k;
   r.renorm = cfg->norm_topk_prob != 0; r.W = (T + 31) / 32;
   r.out_idx = topk_idx; r.out_w = topk_w;
-  return cuda_status(es::launch_route(r, static_cast<cudaStream_t>(stream)));
+  es::DispatchArgs d{};
+  return cuda_status(es::launch_front(r, d, static_cast<cudaStream_t>(stream)));
 }
 
 es_status es_moe_expert_ffn(const es_moe_cfg* cfg, const void* x, const int32_t* topk_idx,
@@ -190,16 +207,17 @@ es_status es_moe_expert_ffn(const es_moe_cfg* cfg, const void* x, const int32_t*
   if (s != ES_OK || T == 0) return s;
   if (!topk_idx || !topk_w) return ES_ERR_INVALID_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(w.bitmap, 0, (size_t)w.E1 * w.W * 4, st) != cudaSuccess) return ES_ERR_CUDA;
   es::RouteArgs r{};
   r.in_idx = topk_idx; r.in_w = topk_w;
   r.x = static_cast<const uint16_t*>(x);
   r.sg_w = static_cast<const uint16_t*>(shared_gate_w);
   r.T = T; r.D = cfg->hidden; r.E = cfg->num_experts; r.k = cfg->top_k;
   r.renorm = cfg->norm_topk_prob != 0; r.has_shared = cfg->shared_inter > 0; r.W = w.W;
-  r.bitmap = w.bitmap; r.sgate = w.sgate; r.x_perm = w.x_perm; r.xsum = w.xsum; r.err = w.err;
-  if (es::launch_route(r, st) != cudaSuccess) return ES_ERR_CUDA;
-  return run_ffn(cfg, w, topk_idx, topk_w, packed, out, out_dtype == ES_DTYPE_F32, T, st);
+  r.sgate = w.sgate; r.x_perm = w.x_perm; r.xsum = w.xsum; r.err = w.err;
+  Marks mk;
+  es_status s2 = run_front(cfg, w, r, topk_idx, topk_w, T, st, mk);
+  if (s2 != ES_OK) return s2;
+  return run_ffn(cfg, w, packed, out, out_dtype == ES_DTYPE_F32, T, st, mk);
 }
 
 es_status es_moe_forward(const es_moe_cfg* cfg, const void* x, const void* logits,
@@ -229,7 +247,6 @@ es_status es_moe_forward_timed(const es_moe_cfg* cfg, const void* x, const void*
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int32_t* idx = topk_idx ? topk_idx : w.topk_idx;
   float* wts = topk_w ? topk_w : w.topk_w;
-  if (cudaMemsetAsync(w.bitmap, 0, (size_t)w.E1 * w.W * 4, st) != cudaSuccess) return ES_ERR_CUDA;
   es::RouteArgs r{};
   r.logits = logits; r.logits_f32 = logits_dtype == ES_DTYPE_F32; r.bias = cache_bias;
   r.x = static_cast<const uint16_t*>(x);
@@ -237,10 +254,10 @@ es_status es_moe_forward_timed(const es_moe_cfg* cfg, const void* x, const void*
   r.T = T; r.D = cfg->hidden; r.E = cfg->num_experts; r.k = cfg->top_k;
   r.renorm = cfg->norm_topk_prob != 0; r.has_shared = cfg->shared_inter > 0; r.W = w.W;
   r.out_idx = idx; r.out_w = wts;
-  r.bitmap = w.bitmap; r.sgate = w.sgate; r.x_perm = w.x_perm; r.xsum = w.xsum; r.err = w.err;
-  if (mk.mark(0, st) != cudaSuccess) return ES_ERR_CUDA;
-  if (es::launch_route(r, st) != cudaSuccess) return ES_ERR_CUDA;
-  return run_ffn(cfg, w, idx, wts, packed, out, out_dtype == ES_DTYPE_F32, T, st, mk);
+  r.sgate = w.sgate; r.x_perm = w.x_perm; r.xsum = w.xsum; r.err = w.err;
+  es_status s2 = run_front(cfg, w, r, idx, wts, T, st, mk);
+  if (s2 != ES_OK) return s2;
+  return run_ffn(cfg, w, packed, out, out_dtype == ES_DTYPE_F32, T, st, mk);
 }
 
 es_status es_moe_read_error(const void* workspace, int32_t clear, uint32_t* flags_out,

@@ -4,8 +4,8 @@
 // Restates engine.py:40-41 ((out * top_k_weights[..., None]).sum(axis=-2))
 // and the shared-expert add of generate.py:173-178. It is a gather: each
 // thread owns four output columns of one token and reads that token's k
-// expert rows, so no floating-point atomics are involved and the sum order
-// is fixed.
+// expert rows in the expert-id order the dispatch recorded, so no
+// floating-point atomics are involved and the sum order is fixed.
 #include "es_common.cuh"
 #include "es_kernels.cuh"
 
@@ -17,35 +17,35 @@ constexpr int kThreads = 256;
 __global__ void __launch_bounds__(kThreads) combine_kernel(CombineArgs a) {
   const int t = blockIdx.y;
   const int d = (blockIdx.x * kThreads + threadIdx.x) * 4;
+  pdl_wait();
+  pdl_trigger();
   if (d >= a.D) return;
-  const int k = a.k, kk = k + (a.has_shared ? 1 : 0);
-  int ids[kMaxTopK];
+  const int k = a.k;
+  // all slot loads first, then all row loads, then the fixed-order sum: the
+  // row loads are independent, so they overlap instead of forming a chain
   int ps[kMaxTopK];
   float ws[kMaxTopK];
-  int m = 0;
-  for (int j = 0; j < k; ++j) {
-    const int e = a.idx[(size_t)t * k + j];
-    const int p = a.pos[(size_t)t * kk + j];
-    if (e < 0 || p < 0) continue;
-    const float w = a.w[(size_t)t * k + j];
-    // insertion by expert id; equal ids keep slot order
-    int i = m++;
-    while (i > 0 && ids[i - 1] > e) {
-      ids[i] = ids[i - 1]; ps[i] = ps[i - 1]; ws[i] = ws[i - 1];
-      --i;
-    }
-    ids[i] = e; ps[i] = p; ws[i] = w;
+#pragma unroll
+  for (int r = 0; r < kMaxTopK; ++r) {
+    ps[r] = r < k ? a.cs_pos[(size_t)t * k + r] : -1;
+    ws[r] = r < k ? a.cs_w[(size_t)t * k + r] : 0.f;
   }
+  float4 ys[kMaxTopK];
+#pragma unroll
+  for (int r = 0; r < kMaxTopK; ++r)
+    ys[r] = ps[r] >= 0 ? *reinterpret_cast<const float4*>(a.y_pair + (size_t)ps[r] * a.D + d)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int i = 0; i < m; ++i) {
-    const float4 y = *reinterpret_cast<const float4*>(a.y_pair + (size_t)ps[i] * a.D + d);
-    acc.x = fmaf(ws[i], y.x, acc.x);
-    acc.y = fmaf(ws[i], y.y, acc.y);
-    acc.z = fmaf(ws[i], y.z, acc.z);
-    acc.w = fmaf(ws[i], y.w, acc.w);
+#pragma unroll
+  for (int r = 0; r < kMaxTopK; ++r) {
+    if (ps[r] < 0) continue;  // masked slots (sorted last) add nothing
+    acc.x = fmaf(ws[r], ys[r].x, acc.x);
+    acc.y = fmaf(ws[r], ys[r].y, acc.y);
+    acc.z = fmaf(ws[r], ys[r].z, acc.z);
+    acc.w = fmaf(ws[r], ys[r].w, acc.w);
   }
   if (a.has_shared) {
-    const int p = a.pos[(size_t)t * kk + k];
+    const int p = a.pos_shared[t];
     const float sg = a.sgate[t];
     const float4 y = *reinterpret_cast<const float4*>(a.y_pair + (size_t)p * a.D + d);
     acc.x = fmaf(sg, y.x, acc.x);
@@ -67,8 +67,7 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(CombineArgs a) {
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st) {
   if (a.T <= 0) return cudaSuccess;
   dim3 grid((a.D / 4 + kThreads - 1) / kThreads, a.T);
-  combine_kernel<<<grid, kThreads, 0, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(combine_kernel, grid, dim3(kThreads), 0, st, a);
 }
 
 }  // namespace es

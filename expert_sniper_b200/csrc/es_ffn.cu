@@ -1,77 +1,210 @@
-// Decode expert FFN: 4-bit dequant-GEMV on register operands.
+// Decode expert FFN: 4-bit dequant-GEMV with warp-independent work items.
 //
 // Restates the three gather_qmm calls of run_expert_ffn
 // (src/mlx_expert_sniper/engine.py:32-39) and the SwiGLU between them
 // (engine.py:37) for every active expert, grouped by expert so each packed
-// weight byte is read from HBM once per call no matter how many tokens chose
-// the expert.
+// weight byte is read from HBM once per call however many tokens chose the
+// expert.
 //
-// Arithmetic. A code q becomes the exact bf16 value 128 + q (es_common.cuh),
-// so the tensor core computes acc = sum_d (128 + q_d) x_d exactly in fp32
-// from bf16 inputs, and per (row, 64-group)
-//     sum_d w_d x_d = scale * acc + (bias - 128 * scale) * sum_d x_d ,
+// Arithmetic. A code q becomes the exact bf16 value 128 + q (gate/up, whose
+// B operand is the bf16 activation) or the exact fp16 value 1024 + q (down,
+// whose B operand is h rounded once to fp16), so the tensor core computes
+// acc = sum_d (c0 + q_d) v_d exactly in fp32, and per (row, 64-group)
+//     sum_d w_d v_d = scale * acc + (bias - c0 * scale) * sum_d v_d ,
 // which is the MLX dequantisation w = scale * q + bias with no rounding of
-// the weights. The group sums of x are precomputed by the router kernel; the
-// down projection takes h as bf16 hi + bf16 lo (two MMAs into one
-// accumulator), keeping h to ~16 bits of mantissa.
+// the weights. |h| beyond the fp16 range is saturated and flagged.
 //
-// Work split. Every warp loads exactly four 64-column groups of one 16-row
-// block (its whole weight share) up front into registers, so at decode sizes
-// each SM has tens of KB of loads in flight. gate/up: a CTA owns (active
-// expert, 16 rows of I); its warps split the D/64 groups and reduce through
-// shared memory, then apply SwiGLU. down: a CTA owns (active expert, R blocks
-// of 16 rows of D); I/256 warps split each block's groups. Tokens of an expert
-// are taken 16 at a time (two n8 tiles) against the weights held in
-// registers, so weights are read once however many tokens chose the expert.
+// Work. An item is (active expert, 16 rows of the output, share of K); one
+// warp owns an item from start to finish: it streams the item's packed tiles
+// in chunks of four 64-column groups through its own ring of shared-memory
+// slots (bulk async copies + one mbarrier per slot, L2 evict-first), converts
+// codes in registers (one LOP3 per pair) and runs m16n8k16 MMAs against up to
+// 16 tokens at a time, looping over further tokens if an expert has more.
+// Warps never wait for each other; items are claimed dynamically from a
+// global counter (so experts with more tokens do not leave a tail), and the
+// lane-0 copy issuer runs kSlots chunks ahead, across item boundaries. For very small batches the K dimension of
+// gate/up is split over KS warps; each writes its partial sums and the last
+// one to arrive (atomic counter, reset after use) adds the KS partials in
+// fixed order before the SwiGLU, so results are deterministic.
 #include "es_common.cuh"
 #include "es_kernels.cuh"
 
 namespace es {
 namespace {
 
-constexpr int kGPW = 4;        // gate/up: groups per warp
-constexpr int kNT = 2;         // n8 token tiles per pass
+constexpr int kGPC = 4;    // 64-column groups per chunk
+constexpr int kSlots = 2;  // ring slots per warp (power of two)
+constexpr int kTiles = 2;  // n8 token tiles per pass: 16 tokens
+constexpr int kGateupWarps = 16;
+constexpr int kDownWarps = 16;
+constexpr int kQueue = 8;  // per-warp queue of claimed items (> kSlots)
+constexpr uint32_t kGateupChunk = kGPC * 2 * kTileBytes;  // gate + up tiles, 4608 B
+constexpr uint32_t kDownChunk = kGPC * kTileBytes;        // 2304 B
+constexpr uint32_t kDevErrTimeout = 0x8u;
+constexpr uint32_t kDevErrRange = 0x10u;
 
-// NWARP * 32 threads at <= 128 registers each (2 CTAs per SM at D = 2048)
-template <int NWARP>
-__global__ void __launch_bounds__(NWARP * 32, NWARP <= 8 ? 16 / NWARP : 1) ffn_gateup_kernel(FfnArgs a) {
-  extern __shared__ __align__(16) float red[];  // [NWARP][kNT][32][8]
+// Per-warp ring of kSlots chunk buffers, one mbarrier each.
+struct WarpRing {
+  uint8_t* buf;
+  uint64_t* bars;
+  uint32_t bytes;
+  uint64_t pol;
+
+  ES_DEV void init() {
+    if ((threadIdx.x & 31) == 0) {
+      for (int s = 0; s < kSlots; ++s) mbar_init(&bars[s], 1);
+      fence_mbar_init();
+    }
+    __syncwarp();
+  }
+  ES_DEV void issue(int q, const void* src) {  // one lane
+    const int s = q & (kSlots - 1);
+    mbar_arrive_expect_tx(&bars[s], bytes);
+    bulk_copy_g2s(buf + (size_t)s * bytes, src, bytes, &bars[s], pol);
+  }
+  ES_DEV const uint8_t* slot(int q) const { return buf + (size_t)(q & (kSlots - 1)) * bytes; }
+  // whole warp; false (after draining this warp's copies in flight) on timeout
+  ES_DEV bool wait(int q, int issued, uint32_t* err) {
+    const bool ok = mbar_wait_bounded(&bars[q & (kSlots - 1)], (q / kSlots) & 1);
+    if (__all_sync(0xffffffffu, ok)) return true;
+    if ((threadIdx.x & 31) == 0) {
+      set_error(err, kDevErrTimeout);
+      for (int r = q; r < issued; ++r) mbar_wait_bounded(&bars[r & (kSlots - 1)], (r / kSlots) & 1);
+    }
+    __syncwarp();
+    return false;
+  }
+};
+
+// Walks the items one warp claims: chunk c of pass p of item i.
+// `per` = items per active expert. Items come from a global counter; the
+// copy-issue cursor claims them (lane 0) and records them in a per-warp
+// queue, which the compute cursor replays in the same order.
+struct Cursor {
+  int n_items;
+  int per, sub;      // per = RB * KS (gate/up) or RBD (down); sub = KS or 1
+  int nch;           // chunks per pass
+  int* queue;        // [kQueue] per-warp claimed item ids (shared memory)
+  int qpos;          // next queue slot this cursor reads or writes
+  int i, ai, rb, ks, e, off, n, np, p, c;
+
+  ES_DEV void load(const FfnArgs& a) {
+    if (i >= n_items) return;
+    ai = i / per;
+    const int rem = i - ai * per;
+    rb = rem / sub;
+    ks = rem - rb * sub;
+    e = a.act_e[ai];
+    off = a.act_off[ai];
+    n = a.act_n[ai];
+    np = (n + kTiles * 8 - 1) / (kTiles * 8);
+    p = 0;
+    c = 0;
+  }
+  // issue side: claim the next item (whole warp)
+  ES_DEV void claim(const FfnArgs& a, int* counter) {
+    int v = 0;
+    if ((threadIdx.x & 31) == 0) {
+      v = atomicAdd(counter, 1);
+      queue[qpos & (kQueue - 1)] = v;
+    }
+    i = __shfl_sync(0xffffffffu, v, 0);
+    ++qpos;
+    load(a);
+  }
+  // compute side: next item from the queue (whole warp)
+  ES_DEV void replay(const FfnArgs& a) {
+    __syncwarp();
+    i = queue[qpos & (kQueue - 1)];
+    ++qpos;
+    load(a);
+  }
+  ES_DEV bool valid() const { return i < n_items; }
+  // advance to the next chunk; at the end of an item, claim/replay the next
+  template <bool kIssue>
+  ES_DEV void advance(const FfnArgs& a, int* counter) {
+    if (++c < nch) return;
+    c = 0;
+    if (++p < np) return;
+    if (kIssue) claim(a, counter); else replay(a);
+  }
+};
+
+
+// ---------------------------------------------------------------------------
+// gate/up + SwiGLU -> h (fp16, fragment order)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kGateupWarps * 32, 1) ffn_gateup_kernel(FfnArgs a, int KS) {
+  extern __shared__ __align__(128) uint8_t smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, c = lane & 3;
   const int GD = a.D / kGroup, RB = a.I / 16;
-  const int ai = blockIdx.x / RB, rb = blockIdx.x - ai * RB;
-  if (ai >= *a.n_active) return;  // block-uniform
-  const int e = a.act_e[ai], off = a.act_off[ai], n = a.act_n[ai];
-  const uint8_t* eb = a.packed + (size_t)e * a.expert_bytes;
+  const int GPI = GD / KS;  // groups per item
+  WarpRing ring{smem + (size_t)warp * kSlots * kGateupChunk,
+                reinterpret_cast<uint64_t*>(smem + (size_t)kGateupWarps * kSlots * kGateupChunk) +
+                    warp * kSlots,
+                kGateupChunk, l2_evict_first_policy()};
+  ring.init();
+  __shared__ int s_queue[kGateupWarps][kQueue];
+  pdl_wait();
+  pdl_trigger();
 
-  uint4 cg[kGPW], cu[kGPW];
-  uint2 sgv[kGPW], suv[kGPW];
-#pragma unroll
-  for (int gi = 0; gi < kGPW; ++gi) {
-    const int G = warp * kGPW + gi;
-    const uint8_t* tg = eb + gateup_tile_off(GD, rb, G, 0);
-    cg[gi] = ld_stream16(tg + lane * 16);
-    cu[gi] = ld_stream16(tg + kTileBytes + lane * 16);
-    sgv[gi] = ld_stream8(tg + kTileCodeBytes + g * 8);
-    suv[gi] = ld_stream8(tg + kTileBytes + kTileCodeBytes + g * 8);
+  const int n_items = *a.n_active * RB * KS;
+  Cursor ic{n_items, RB * KS, KS, GPI / kGPC, s_queue[warp], 0};
+  ic.claim(a, &a.item_ctr[0]);
+  Cursor cc = ic;
+  cc.qpos = 0;
+  cc.replay(a);
+  if (!cc.valid()) return;
+  auto src = [&](const Cursor& u) {
+    return a.packed + (size_t)u.e * a.expert_bytes +
+           gateup_tile_off(GD, u.rb, u.ks * GPI + u.c * kGPC, 0);
+  };
+  int issued = 0;
+  for (; issued < kSlots && ic.valid(); ++issued) {
+    if (lane == 0) ring.issue(issued, src(ic));
+    ic.advance<true>(a, &a.item_ctr[0]);
   }
 
-  for (int base = 0; base < n; base += kNT * 8) {
-    float ag[kNT][4], au[kNT][4];
-    int tb[kNT], tc0[kNT], tc1[kNT];
+  float acc[kTiles][8];
+  int tb[kTiles], tc0[kTiles], tc1[kTiles];
+  int ntile = 0;
+  for (int q = 0; cc.valid(); ++q) {
+    if (cc.c == 0) {  // start of a pass over 32 tokens
+      const int base = cc.p * kTiles * 8;
+      ntile = min(kTiles, (cc.n - base + 7) / 8);
 #pragma unroll
-    for (int nt = 0; nt < kNT; ++nt) {
+      for (int t = 0; t < kTiles; ++t) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) { ag[nt][i] = 0.f; au[nt][i] = 0.f; }
-      const int colb = base + nt * 8 + g;
-      const int colc = base + nt * 8 + 2 * c;
-      tb[nt] = colb < n ? a.pair_tok[off + colb] : -1;
-      tc0[nt] = colc < n ? a.pair_tok[off + colc] : -1;
-      tc1[nt] = colc + 1 < n ? a.pair_tok[off + colc + 1] : -1;
+        for (int v = 0; v < 8; ++v) acc[t][v] = 0.f;
+        const int cb = base + t * 8 + g, cq = base + t * 8 + 2 * c;
+        tb[t] = cb < cc.n ? a.pair_tok[cc.off + cb] : -1;
+        tc0[t] = cq < cc.n ? a.pair_tok[cc.off + cq] : -1;
+        tc1[t] = cq + 1 < cc.n ? a.pair_tok[cc.off + cq + 1] : -1;
+      }
     }
+    if (!ring.wait(q, issued, a.err)) return;
+    const uint8_t* st = ring.slot(q);
+    uint4 cg[kGPC], cu[kGPC];
+    uint2 sgv[kGPC], suv[kGPC];
 #pragma unroll
-    for (int gi = 0; gi < kGPW; ++gi) {
-      const int G = warp * kGPW + gi;
+    for (int gi = 0; gi < kGPC; ++gi) {
+      const uint8_t* tg = st + (size_t)(gi * 2) * kTileBytes;
+      cg[gi] = ld_shared16(tg + lane * 16);
+      cu[gi] = ld_shared16(tg + kTileBytes + lane * 16);
+      sgv[gi] = ld_shared8(tg + kTileCodeBytes + g * 8);
+      suv[gi] = ld_shared8(tg + kTileBytes + kTileCodeBytes + g * 8);
+    }
+    __syncwarp();  // slot consumed by every lane: refill it
+    if (ic.valid()) {
+      if (lane == 0) ring.issue(issued, src(ic));
+      ic.advance<true>(a, &a.item_ctr[0]);
+      ++issued;
+    }
+    const int G0 = cc.ks * GPI + cc.c * kGPC;
+#pragma unroll
+    for (int gi = 0; gi < kGPC; ++gi) {
+      const int G = G0 + gi;
       const float gs0 = lo_half_f(sgv[gi].x), gs8 = lo_half_f(sgv[gi].y);
       const float gb0 = fmaf(-128.f, gs0, hi_half_f(sgv[gi].x));
       const float gb8 = fmaf(-128.f, gs8, hi_half_f(sgv[gi].y));
@@ -79,235 +212,269 @@ __global__ void __launch_bounds__(NWARP * 32, NWARP <= 8 ? 16 / NWARP : 1) ffn_g
       const float ub0 = fmaf(-128.f, us0, hi_half_f(suv[gi].x));
       const float ub8 = fmaf(-128.f, us8, hi_half_f(suv[gi].y));
       // A operands of the four k-steps: rows g (words .x, .y) and g + 8 (.z, .w)
-      uint32_t ag_op[4][4], au_op[4][4];
+      uint32_t ag[4][4], au[4][4];
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        ag_op[s][0] = code_pair(cg[gi].x, s); ag_op[s][1] = code_pair(cg[gi].z, s);
-        ag_op[s][2] = code_pair(cg[gi].y, s); ag_op[s][3] = code_pair(cg[gi].w, s);
-        au_op[s][0] = code_pair(cu[gi].x, s); au_op[s][1] = code_pair(cu[gi].z, s);
-        au_op[s][2] = code_pair(cu[gi].y, s); au_op[s][3] = code_pair(cu[gi].w, s);
+        ag[s][0] = code_pair(cg[gi].x, s); ag[s][1] = code_pair(cg[gi].z, s);
+        ag[s][2] = code_pair(cg[gi].y, s); ag[s][3] = code_pair(cg[gi].w, s);
+        au[s][0] = code_pair(cu[gi].x, s); au[s][1] = code_pair(cu[gi].z, s);
+        au[s][2] = code_pair(cu[gi].y, s); au[s][3] = code_pair(cu[gi].w, s);
       }
 #pragma unroll
-      for (int nt = 0; nt < kNT; ++nt) {
-        uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
-        if (tb[nt] >= 0) {
-          const uint4* xp = reinterpret_cast<const uint4*>(a.x_perm + ((size_t)tb[nt] * GD + G) * kGroup + c * 16);
+      for (int t = 0; t < kTiles; ++t) {
+        if (t >= ntile) break;  // warp-uniform
+        uint4 xa = make_uint4(0, 0, 0, 0), xb = xa;
+        if (tb[t] >= 0) {
+          const uint4* xp = reinterpret_cast<const uint4*>(a.x_perm + ((size_t)tb[t] * GD + G) * kGroup + c * 16);
           xa = __ldg(xp);
           xb = __ldg(xp + 1);
         }
-        const float xs0 = tc0[nt] >= 0 ? __ldg(a.xsum + (size_t)tc0[nt] * GD + G) : 0.f;
-        const float xs1 = tc1[nt] >= 0 ? __ldg(a.xsum + (size_t)tc1[nt] * GD + G) : 0.f;
+        const float xs0 = tc0[t] >= 0 ? __ldg(a.xsum + (size_t)tc0[t] * GD + G) : 0.f;
+        const float xs1 = tc1[t] >= 0 ? __ldg(a.xsum + (size_t)tc1[t] * GD + G) : 0.f;
         const uint32_t bw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
         float tg[4] = {0.f, 0.f, 0.f, 0.f}, tu[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int s = 0; s < 4; ++s) {
-          mma_bf16(tg, ag_op[s][0], ag_op[s][1], ag_op[s][2], ag_op[s][3], bw[2 * s], bw[2 * s + 1], tg);
-          mma_bf16(tu, au_op[s][0], au_op[s][1], au_op[s][2], au_op[s][3], bw[2 * s], bw[2 * s + 1], tu);
+          mma_bf16(tg, ag[s][0], ag[s][1], ag[s][2], ag[s][3], bw[2 * s], bw[2 * s + 1], tg);
+          mma_bf16(tu, au[s][0], au[s][1], au[s][2], au[s][3], bw[2 * s], bw[2 * s + 1], tu);
         }
-        ag[nt][0] = fmaf(gs0, tg[0], fmaf(gb0, xs0, ag[nt][0]));
-        ag[nt][1] = fmaf(gs0, tg[1], fmaf(gb0, xs1, ag[nt][1]));
-        ag[nt][2] = fmaf(gs8, tg[2], fmaf(gb8, xs0, ag[nt][2]));
-        ag[nt][3] = fmaf(gs8, tg[3], fmaf(gb8, xs1, ag[nt][3]));
-        au[nt][0] = fmaf(us0, tu[0], fmaf(ub0, xs0, au[nt][0]));
-        au[nt][1] = fmaf(us0, tu[1], fmaf(ub0, xs1, au[nt][1]));
-        au[nt][2] = fmaf(us8, tu[2], fmaf(ub8, xs0, au[nt][2]));
-        au[nt][3] = fmaf(us8, tu[3], fmaf(ub8, xs1, au[nt][3]));
+        acc[t][0] = fmaf(gs0, tg[0], fmaf(gb0, xs0, acc[t][0]));
+        acc[t][1] = fmaf(gs0, tg[1], fmaf(gb0, xs1, acc[t][1]));
+        acc[t][2] = fmaf(gs8, tg[2], fmaf(gb8, xs0, acc[t][2]));
+        acc[t][3] = fmaf(gs8, tg[3], fmaf(gb8, xs1, acc[t][3]));
+        acc[t][4] = fmaf(us0, tu[0], fmaf(ub0, xs0, acc[t][4]));
+        acc[t][5] = fmaf(us0, tu[1], fmaf(ub0, xs1, acc[t][5]));
+        acc[t][6] = fmaf(us8, tu[2], fmaf(ub8, xs0, acc[t][6]));
+        acc[t][7] = fmaf(us8, tu[3], fmaf(ub8, xs1, acc[t][7]));
       }
     }
-    // cross-warp reduction of the K split
+
+    if (cc.c == cc.nch - 1) {  // end of the pass: SwiGLU -> h
+      bool last = true;
+      if (KS > 1) {  // only for batches of <= 8 tokens: one pass, one tile
+        const int slot = cc.ai * RB + cc.rb;
+        float4* part = reinterpret_cast<float4*>(a.partials) + ((size_t)slot * KS + cc.ks) * 64;
+        part[lane * 2] = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+        part[lane * 2 + 1] = make_float4(acc[0][4], acc[0][5], acc[0][6], acc[0][7]);
+        __threadfence();
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) old = atomicAdd(&a.counters[slot], 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        last = old == KS - 1;
+        if (last) {
+          __threadfence();
 #pragma unroll
-    for (int nt = 0; nt < kNT; ++nt) {
-      float4* r = reinterpret_cast<float4*>(red + (((size_t)warp * kNT + nt) * 32 + lane) * 8);
-      r[0] = make_float4(ag[nt][0], ag[nt][1], ag[nt][2], ag[nt][3]);
-      r[1] = make_float4(au[nt][0], au[nt][1], au[nt][2], au[nt][3]);
-    }
-    __syncthreads();
-    if (threadIdx.x < kNT * 32) {
-      const int nt = threadIdx.x >> 5, ln = threadIdx.x & 31;
-      float gsum[4] = {0.f, 0.f, 0.f, 0.f}, usum[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int w = 0; w < NWARP; ++w) {
-        const float4* q = reinterpret_cast<const float4*>(red + (((size_t)w * kNT + nt) * 32 + ln) * 8);
-        const float4 q0 = q[0], q1 = q[1];
-        gsum[0] += q0.x; gsum[1] += q0.y; gsum[2] += q0.z; gsum[3] += q0.w;
-        usum[0] += q1.x; usum[1] += q1.y; usum[2] += q1.z; usum[3] += q1.w;
-      }
-      const int g2 = ln >> 2, c2 = ln & 3;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int row = (i < 2) ? g2 : g2 + 8;
-        const int col = base + nt * 8 + 2 * c2 + (i & 1);
-        if (col < n) {
-          const float gv = gsum[i];
-          const float h = gv / (1.f + expf(-gv)) * usum[i];
-          const uint16_t hi = float_to_bf16_bits(h);
-          const uint16_t lo = float_to_bf16_bits(h - bf16_bits_to_float(hi));
-          const size_t idx = (size_t)(off + col) * a.I + frag_pos(rb * 16 + row);
-          a.h_hi[idx] = hi;
-          a.h_lo[idx] = lo;
+          for (int v = 0; v < 8; ++v) acc[0][v] = 0.f;
+          const float4* pp = reinterpret_cast<const float4*>(a.partials) + (size_t)slot * KS * 64;
+          for (int k2 = 0; k2 < KS; ++k2) {  // fixed order: deterministic
+            const float4 p0 = __ldcg(pp + (size_t)k2 * 64 + lane * 2);
+            const float4 p1 = __ldcg(pp + (size_t)k2 * 64 + lane * 2 + 1);
+            acc[0][0] += p0.x; acc[0][1] += p0.y; acc[0][2] += p0.z; acc[0][3] += p0.w;
+            acc[0][4] += p1.x; acc[0][5] += p1.y; acc[0][6] += p1.z; acc[0][7] += p1.w;
+          }
+          if (lane == 0) a.counters[slot] = 0;
         }
       }
+      if (last) {
+        const int base = cc.p * kTiles * 8;
+#pragma unroll
+        for (int t = 0; t < kTiles; ++t) {
+          if (t >= ntile) break;
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const int row = (v < 2) ? g : g + 8;
+            const int col = base + t * 8 + 2 * c + (v & 1);
+            if (col < cc.n) {
+              const float gv = acc[t][v];
+              float h = gv / (1.f + expf(-gv)) * acc[t][4 + v];
+              if (!(fabsf(h) <= 65504.f)) {  // outside fp16 (or NaN): saturate, flag
+                set_error(a.err, kDevErrRange);
+                h = h != h ? 0.f : copysignf(65504.f, h);
+              }
+              a.h16[(size_t)(cc.off + col) * a.I + frag_pos(cc.rb * 16 + row)] =
+                  __half_as_ushort(__float2half_rn(h));
+            }
+          }
+        }
+      }
     }
-    __syncthreads();
+    cc.advance<false>(a, nullptr);
   }
 }
 
-// down: R row blocks per CTA, KC warps per row block, each warp 4 groups of I.
-template <int KC>
-struct DownShape {
-  static constexpr int R = KC <= 4 ? 4 : 2;
-  static constexpr int WARPS = R * KC;
-};
-
-template <int KC>
-__global__ void __launch_bounds__(DownShape<KC>::WARPS * 32) ffn_down_kernel(FfnArgs a) {
-  constexpr int R = DownShape<KC>::R;
-  extern __shared__ __align__(16) float red[];  // [R*KC][kNT][32][4]
+// ---------------------------------------------------------------------------
+// down -> y per (token, slot)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kDownWarps * 32, 1) ffn_down_kernel(FfnArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
   const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, c = lane & 3;
-  const int rbl = warp / KC, kc = warp - rbl * KC;
-  const int CPB = (a.D / 16) / R;  // CTAs per expert
-  const int ai = blockIdx.x / CPB;
-  const int rb = (blockIdx.x - ai * CPB) * R + rbl;
-  if (ai >= *a.n_active) return;  // block-uniform
-  const int e = a.act_e[ai], off = a.act_off[ai], n = a.act_n[ai];
-  const uint8_t* tb = a.packed + (size_t)e * a.expert_bytes + down_tile_off(a.D, a.I, rb, kc * kGPW);
-
-  uint4 cw[kGPW];
-  uint2 sw[kGPW];
-#pragma unroll
-  for (int gi = 0; gi < kGPW; ++gi) {
-    cw[gi] = ld_stream16(tb + (size_t)gi * kTileBytes + lane * 16);
-    sw[gi] = ld_stream8(tb + (size_t)gi * kTileBytes + kTileCodeBytes + g * 8);
+  const int KG = a.I / kGroup, RBD = a.D / 16;
+  WarpRing ring{smem + (size_t)warp * kSlots * kDownChunk,
+                reinterpret_cast<uint64_t*>(smem + (size_t)kDownWarps * kSlots * kDownChunk) +
+                    warp * kSlots,
+                kDownChunk, l2_evict_first_policy()};
+  ring.init();
+  // The expert list comes from the front-end kernel, which completed before
+  // the gate/up kernel (this kernel's predecessor) passed its own
+  // pdl_wait(), so the first weight copies can be in flight while gate/up
+  // finishes; only h (written by gate/up) needs pdl_wait().
+  __shared__ int s_queue[kDownWarps][kQueue];
+  const int n_items = *a.n_active * RBD;
+  Cursor ic{n_items, RBD, 1, KG / kGPC, s_queue[warp], 0};
+  ic.claim(a, &a.item_ctr[1]);
+  Cursor cc = ic;
+  cc.qpos = 0;
+  cc.replay(a);
+  const bool any = cc.valid();
+  auto src = [&](const Cursor& u) {
+    return a.packed + (size_t)u.e * a.expert_bytes + down_tile_off(a.D, a.I, u.rb, u.c * kGPC);
+  };
+  int issued = 0;
+  for (; any && issued < kSlots && ic.valid(); ++issued) {
+    if (lane == 0) ring.issue(issued, src(ic));
+    ic.advance<true>(a, &a.item_ctr[1]);
   }
+  pdl_wait();
+  pdl_trigger();
+  if (!any) return;
 
-  for (int base = 0; base < n; base += kNT * 8) {
-    float acc[kNT][4];
-    int pb[kNT];
+  float acc[kTiles][4];
+  int pb[kTiles];
+  int ntile = 0;
+  for (int q = 0; cc.valid(); ++q) {
+    if (cc.c == 0) {
+      const int base = cc.p * kTiles * 8;
+      ntile = min(kTiles, (cc.n - base + 7) / 8);
 #pragma unroll
-    for (int nt = 0; nt < kNT; ++nt) {
+      for (int t = 0; t < kTiles; ++t) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
-      const int col = base + nt * 8 + g;
-      pb[nt] = col < n ? off + col : -1;
+        for (int v = 0; v < 4; ++v) acc[t][v] = 0.f;
+        const int col = base + t * 8 + g;
+        pb[t] = col < cc.n ? cc.off + col : -1;
+      }
     }
+    if (!ring.wait(q, issued, a.err)) return;
+    const uint8_t* st = ring.slot(q);
+    uint4 cw[kGPC];
+    uint2 sw[kGPC];
 #pragma unroll
-    for (int gi = 0; gi < kGPW; ++gi) {
-      const int G = kc * kGPW + gi;
+    for (int gi = 0; gi < kGPC; ++gi) {
+      cw[gi] = ld_shared16(st + (size_t)gi * kTileBytes + lane * 16);
+      sw[gi] = ld_shared8(st + (size_t)gi * kTileBytes + kTileCodeBytes + g * 8);
+    }
+    __syncwarp();
+    if (ic.valid()) {
+      if (lane == 0) ring.issue(issued, src(ic));
+      ic.advance<true>(a, &a.item_ctr[1]);
+      ++issued;
+    }
+    const int G0 = cc.c * kGPC;
+#pragma unroll
+    for (int gi = 0; gi < kGPC; ++gi) {
+      const int G = G0 + gi;
       const float s0 = lo_half_f(sw[gi].x), s8 = lo_half_f(sw[gi].y);
-      const float b0 = fmaf(-128.f, s0, hi_half_f(sw[gi].x));
-      const float b8 = fmaf(-128.f, s8, hi_half_f(sw[gi].y));
-      uint32_t a_op[4][4];
+      const float b0 = fmaf(-1024.f, s0, hi_half_f(sw[gi].x));
+      const float b8 = fmaf(-1024.f, s8, hi_half_f(sw[gi].y));
+      uint32_t ao[4][4];
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        a_op[s][0] = code_pair(cw[gi].x, s); a_op[s][1] = code_pair(cw[gi].z, s);
-        a_op[s][2] = code_pair(cw[gi].y, s); a_op[s][3] = code_pair(cw[gi].w, s);
+        ao[s][0] = code_pair_f16(cw[gi].x, s); ao[s][1] = code_pair_f16(cw[gi].z, s);
+        ao[s][2] = code_pair_f16(cw[gi].y, s); ao[s][3] = code_pair_f16(cw[gi].w, s);
       }
 #pragma unroll
-      for (int nt = 0; nt < kNT; ++nt) {
-        uint4 h0 = make_uint4(0, 0, 0, 0), h1 = h0, l0 = h0, l1 = h0;
-        if (pb[nt] >= 0) {
-          const size_t o = (size_t)pb[nt] * a.I + G * kGroup + c * 16;
-          const uint4* hp = reinterpret_cast<const uint4*>(a.h_hi + o);
-          const uint4* lp = reinterpret_cast<const uint4*>(a.h_lo + o);
-          h0 = hp[0]; h1 = hp[1]; l0 = lp[0]; l1 = lp[1];
+      for (int t = 0; t < kTiles; ++t) {
+        if (t >= ntile) break;  // warp-uniform
+        uint4 h0 = make_uint4(0, 0, 0, 0), h1 = h0;
+        if (pb[t] >= 0) {
+          const uint4* hp = reinterpret_cast<const uint4*>(a.h16 + (size_t)pb[t] * a.I + G * kGroup + c * 16);
+          h0 = hp[0];
+          h1 = hp[1];
         }
         const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-        const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
         float hs = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          hs += bf16_bits_to_float(hw[i] & 0xffffu) + bf16_bits_to_float(hw[i] >> 16);
-          hs += bf16_bits_to_float(lw[i] & 0xffffu) + bf16_bits_to_float(lw[i] >> 16);
-        }
+        for (int v = 0; v < 8; ++v) hs += lo_half_f(hw[v]) + hi_half_f(hw[v]);
         hs += __shfl_xor_sync(full, hs, 1);
         hs += __shfl_xor_sync(full, hs, 2);
         const float hs0 = __shfl_sync(full, hs, (2 * c) << 2);
         const float hs1 = __shfl_sync(full, hs, (2 * c + 1) << 2);
         float tmp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          mma_bf16(tmp, a_op[s][0], a_op[s][1], a_op[s][2], a_op[s][3], hw[2 * s], hw[2 * s + 1], tmp);
-          mma_bf16(tmp, a_op[s][0], a_op[s][1], a_op[s][2], a_op[s][3], lw[2 * s], lw[2 * s + 1], tmp);
-        }
-        acc[nt][0] = fmaf(s0, tmp[0], fmaf(b0, hs0, acc[nt][0]));
-        acc[nt][1] = fmaf(s0, tmp[1], fmaf(b0, hs1, acc[nt][1]));
-        acc[nt][2] = fmaf(s8, tmp[2], fmaf(b8, hs0, acc[nt][2]));
-        acc[nt][3] = fmaf(s8, tmp[3], fmaf(b8, hs1, acc[nt][3]));
+        for (int s = 0; s < 4; ++s)
+          mma_f16(tmp, ao[s][0], ao[s][1], ao[s][2], ao[s][3], hw[2 * s], hw[2 * s + 1], tmp);
+        acc[t][0] = fmaf(s0, tmp[0], fmaf(b0, hs0, acc[t][0]));
+        acc[t][1] = fmaf(s0, tmp[1], fmaf(b0, hs1, acc[t][1]));
+        acc[t][2] = fmaf(s8, tmp[2], fmaf(b8, hs0, acc[t][2]));
+        acc[t][3] = fmaf(s8, tmp[3], fmaf(b8, hs1, acc[t][3]));
       }
     }
-    // reduce the KC partial sums of each row block, in kc order
+    if (cc.c == cc.nch - 1) {  // end of the pass: store y rows
+      const int base = cc.p * kTiles * 8;
 #pragma unroll
-    for (int nt = 0; nt < kNT; ++nt)
-      reinterpret_cast<float4*>(red)[((size_t)warp * kNT + nt) * 32 + lane] =
-          make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
-    __syncthreads();
-    if (threadIdx.x < R * kNT * 32) {
-      const int r2 = threadIdx.x / (kNT * 32);
-      const int nt = (threadIdx.x >> 5) % kNT, ln = threadIdx.x & 31;
-      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int k2 = 0; k2 < KC; ++k2) {
-        const float4 q = reinterpret_cast<const float4*>(red)[((size_t)(r2 * KC + k2) * kNT + nt) * 32 + ln];
-        sum.x += q.x; sum.y += q.y; sum.z += q.z; sum.w += q.w;
+      for (int t = 0; t < kTiles; ++t) {
+        if (t >= ntile) break;
+        const int col = base + t * 8 + 2 * c;
+        float* y0 = a.y_pair + (size_t)(cc.off + col) * a.D + cc.rb * 16;
+        if (col < cc.n) { y0[g] = acc[t][0]; y0[g + 8] = acc[t][2]; }
+        if (col + 1 < cc.n) { y0[a.D + g] = acc[t][1]; y0[a.D + g + 8] = acc[t][3]; }
       }
-      const int g2 = ln >> 2, c2 = ln & 3;
-      const int rbo = (blockIdx.x - ai * CPB) * R + r2;
-      const int col = base + nt * 8 + 2 * c2;
-      float* y0 = a.y_pair + (size_t)(off + col) * a.D + rbo * 16;
-      if (col < n) { y0[g2] = sum.x; y0[g2 + 8] = sum.z; }
-      if (col + 1 < n) { y0[a.D + g2] = sum.y; y0[a.D + g2 + 8] = sum.w; }
     }
-    __syncthreads();
+    cc.advance<false>(a, nullptr);
   }
 }
 
-template <int NWARP>
-cudaError_t launch_gateup_nw(const FfnArgs& a, int max_active, cudaStream_t st) {
-  const size_t smem = (size_t)NWARP * kNT * 32 * 8 * sizeof(float);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(ffn_gateup_kernel<NWARP>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-  }
-  ffn_gateup_kernel<NWARP><<<max_active * (a.I / 16), NWARP * 32, smem, st>>>(a);
-  return cudaGetLastError();
-}
-
-template <int KC>
-cudaError_t launch_down_kc(const FfnArgs& a, int max_active, cudaStream_t st) {
-  constexpr int R = DownShape<KC>::R, WARPS = DownShape<KC>::WARPS;
-  const int CPB = (a.D / 16) / R;
-  const size_t smem = (size_t)WARPS * kNT * 32 * 4 * sizeof(float);
-  ffn_down_kernel<KC><<<max_active * CPB, WARPS * 32, smem, st>>>(a);
-  return cudaGetLastError();
+template <typename K, typename... Args>
+cudaError_t launch_ring_kernel(K kernel, int warps, uint32_t chunk, int max_items,
+                               cudaStream_t st, Args... args) {
+  const size_t smem = (size_t)warps * kSlots * (chunk + 8);
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  int grid = sm_count();
+  const int need = (max_items + warps - 1) / warps;
+  if (grid > need) grid = need;
+  if (grid < 1) grid = 1;
+  // items are claimed from a counter the front end zeroed
+  return launch_pdl(kernel, dim3(grid), dim3(warps * 32), smem, st, args...);
 }
 
 }  // namespace
 
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!cached[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = v > 0 ? v : 148;
+  }
+  return cached[dev];
+}
+
+int ffn_split_k(int T, int max_active, int D, int I) {
+  const int GD = D / kGroup, RB = I / 16;
+  if (T > kSplitKMaxTokens) return 1;
+  const int warps = sm_count() * kGateupWarps;
+  int ks = 1;
+  while (ks < kMaxSplitK && GD % (ks * 2 * kGPC) == 0 && (long long)max_active * RB * ks < warps)
+    ks *= 2;
+  return ks;
+}
+
 cudaError_t launch_ffn_gateup(const FfnArgs& a, int max_active, cudaStream_t st) {
   if (max_active <= 0) return cudaSuccess;
-  switch ((a.D / kGroup) / kGPW) {
-    case 1: return launch_gateup_nw<1>(a, max_active, st);
-    case 2: return launch_gateup_nw<2>(a, max_active, st);
-    case 4: return launch_gateup_nw<4>(a, max_active, st);
-    case 8: return launch_gateup_nw<8>(a, max_active, st);
-    case 16: return launch_gateup_nw<16>(a, max_active, st);
-    default: return cudaErrorInvalidValue;
-  }
+  const int KS = a.split_k;
+  return launch_ring_kernel(ffn_gateup_kernel, kGateupWarps, kGateupChunk,
+                            max_active * (a.I / 16) * KS, st, a, KS);
 }
 
 cudaError_t launch_ffn_down(const FfnArgs& a, int max_active, cudaStream_t st) {
   if (max_active <= 0) return cudaSuccess;
-  switch ((a.I / kGroup) / kGPW) {
-    case 1: return launch_down_kc<1>(a, max_active, st);
-    case 2: return launch_down_kc<2>(a, max_active, st);
-    case 3: return launch_down_kc<3>(a, max_active, st);
-    case 4: return launch_down_kc<4>(a, max_active, st);
-    case 6: return launch_down_kc<6>(a, max_active, st);
-    case 8: return launch_down_kc<8>(a, max_active, st);
-    default: return cudaErrorInvalidValue;
-  }
+  return launch_ring_kernel(ffn_down_kernel, kDownWarps, kDownChunk, max_active * (a.D / 16), st, a);
 }
 
 }  // namespace es

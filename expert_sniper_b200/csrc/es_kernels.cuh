@@ -30,16 +30,21 @@ struct RouteArgs {
 };
 
 struct DispatchArgs {
-  const uint32_t* bitmap;
+  const uint32_t* bitmap;   // [E1][W]
   const int32_t* idx;       // [T][k]
+  const float* w;           // [T][k]
   int T, E, k, has_shared, W;
-  int32_t* wpre;
+  int32_t* wpre;            // [E1][W]
   int32_t* n_active;
   int32_t* act_e;
   int32_t* act_off;
   int32_t* act_n;
   int32_t* pair_tok;
-  int32_t* pos;             // [T][kk]
+  int32_t* pos_shared;      // [T] pair of the shared expert
+  int32_t* cs_pos;          // [T][k] sorted pair of the r-th smallest expert id, -1 = none
+  float* cs_w;              // [T][k] its routing weight
+  int* ticket;              // CTAs done routing (zero between calls)
+  int* item_ctr;            // [2] FFN work counters, zeroed here for the FFN kernels
 };
 
 struct FfnArgs {
@@ -53,15 +58,19 @@ struct FfnArgs {
   const int32_t* pair_tok;
   const uint16_t* x_perm;
   const float* xsum;
-  uint16_t* h_hi;
-  uint16_t* h_lo;
+  uint16_t* h16;            // [P][I] fp16, fragment order
   float* y_pair;
+  uint32_t* err;
+  float* partials;          // split-K partial sums (split_k > 1)
+  int* counters;            // split-K arrival counters, zero between calls
+  int* item_ctr;            // [2] dynamic item counters (gate/up, down)
+  int split_k;
 };
 
 struct CombineArgs {
-  const int32_t* idx;       // [T][k]
-  const float* w;           // [T][k]
-  const int32_t* pos;       // [T][kk]
+  const int32_t* cs_pos;    // [T][k]
+  const float* cs_w;        // [T][k]
+  const int32_t* pos_shared;  // [T]
   const float* sgate;       // [T]
   const float* y_pair;      // [P][D]
   int T, D, k, has_shared;
@@ -82,8 +91,28 @@ struct PrepareArgs {
   uint8_t* packed;
 };
 
-cudaError_t launch_route(const RouteArgs& a, cudaStream_t st);
-cudaError_t launch_dispatch(const DispatchArgs& a, cudaStream_t st);
+// Launch with programmatic stream serialization (see pdl_wait in es_common.cuh).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// router (+ operand prep + dispatch when r.bitmap is set), one launch
+cudaError_t launch_front(const RouteArgs& r, const DispatchArgs& d, cudaStream_t st);
+int sm_count();
+// K split of gate/up items for a batch of T tokens (1 above kSplitKMaxTokens)
+int ffn_split_k(int T, int max_active, int D, int I);
 cudaError_t launch_ffn_gateup(const FfnArgs& a, int max_active, cudaStream_t st);
 cudaError_t launch_ffn_down(const FfnArgs& a, int max_active, cudaStream_t st);
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);

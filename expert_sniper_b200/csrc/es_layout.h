@@ -39,6 +39,8 @@ constexpr int kTileBytes = 576;
 constexpr int kTileCodeBytes = 512;
 constexpr int kMaxTopK = 16;
 constexpr int kMaxExperts = 1024;
+constexpr int kMaxSplitK = 8;         // K split of gate/up items for tiny batches
+constexpr int kSplitKMaxTokens = 8;   // ... used only up to this many tokens
 
 __host__ __device__ inline size_t expert_bytes(int D, int I) {
   return (size_t)3 * D * I * 9 / 16;
@@ -70,15 +72,20 @@ struct Workspace {
   int32_t* act_off;    // [E1]      first sorted pair of each active expert
   int32_t* act_n;      // [E1]      pairs of each active expert
   int32_t* pair_tok;   // [P]       token of each sorted pair
-  int32_t* pos;        // [T][kk]   sorted pair of (token, slot), -1 = none
+  int32_t* pos;        // [T]       pair of the shared expert
+  int32_t* cs_pos;     // [T][k]    pairs of a token in expert id order
+  float* cs_w;         // [T][k]    their weights
   int32_t* topk_idx;   // [T][k]
   float* topk_w;       // [T][k]
   float* sgate;        // [T]       shared-expert gate
   uint16_t* x_perm;    // [T][D]    bf16, fragment order
   float* xsum;         // [T][D/64]
-  uint16_t* h_hi;      // [P][I]    bf16 high part of h, fragment order
-  uint16_t* h_lo;      // [P][I]    bf16 remainder h - hi
+  uint16_t* h16;       // [P][I]    fp16 h, fragment order
   float* y_pair;       // [P][D]
+  float* partials;     // [A][I/16][kMaxSplitK][256]  split-K partials (T <= 8)
+  int* counters;       // [A][I/16]  split-K arrivals; zero between calls
+  int* ticket;         // front-end CTAs done; zero between calls
+  int* item_ctr;       // [2] FFN work counters
   int W, P, kk, E1;
   size_t bytes;
 };
@@ -99,6 +106,7 @@ inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
     return o;
   };
   size_t o_err = take(256);
+  size_t o_ctl = take(256);
   size_t o_bitmap = take((size_t)E1 * W * 4);
   size_t o_wpre = take((size_t)E1 * W * 4);
   size_t o_nact = take(4);
@@ -107,14 +115,24 @@ inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
   size_t o_actn = take((size_t)E1 * 4);
   size_t o_ptok = take((size_t)P * 4);
   size_t o_pos = take((size_t)Tm * kk * 4);
+  size_t o_cspos = take((size_t)Tm * k * 4);
+  size_t o_csw = take((size_t)Tm * k * 4);
   size_t o_tidx = take((size_t)Tm * k * 4);
   size_t o_tw = take((size_t)Tm * k * 4);
   size_t o_sg = take((size_t)Tm * 4);
   size_t o_xp = take((size_t)Tm * D * 2);
   size_t o_xs = take((size_t)Tm * (D / kGroup) * 4);
   size_t o_hh = take((size_t)P * I * 2);
-  size_t o_hl = take((size_t)P * I * 2);
   size_t o_y = take((size_t)P * D * 4);
+  const long long routed = (long long)Tm * k < E ? (long long)Tm * k : E;
+  const size_t A = (size_t)routed + (has_shared ? 1 : 0);  // most active experts
+  // split-K partials are used up to kSplitKMaxTokens tokens; larger T keeps
+  // that amount so the size never shrinks as T grows
+  const long long Ts = Tm < kSplitKMaxTokens ? Tm : kSplitKMaxTokens;
+  const size_t As = (size_t)((Ts * k < E ? Ts * k : E) + (has_shared ? 1 : 0));
+  const size_t part_items = As * (I / 16) * kMaxSplitK;
+  size_t o_part = take(part_items * 256 * 4);
+  size_t o_cnt = take(A * (I / 16) * 4);
   w.bytes = off;
   w.W = W;
   w.P = P;
@@ -123,6 +141,8 @@ inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
   if (base) {
     char* b = static_cast<char*>(base);
     w.err = reinterpret_cast<uint32_t*>(b + o_err);
+    w.ticket = reinterpret_cast<int*>(b + o_ctl);
+    w.item_ctr = reinterpret_cast<int*>(b + o_ctl) + 1;
     w.bitmap = reinterpret_cast<uint32_t*>(b + o_bitmap);
     w.wpre = reinterpret_cast<int32_t*>(b + o_wpre);
     w.n_active = reinterpret_cast<int32_t*>(b + o_nact);
@@ -131,14 +151,17 @@ inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
     w.act_n = reinterpret_cast<int32_t*>(b + o_actn);
     w.pair_tok = reinterpret_cast<int32_t*>(b + o_ptok);
     w.pos = reinterpret_cast<int32_t*>(b + o_pos);
+    w.cs_pos = reinterpret_cast<int32_t*>(b + o_cspos);
+    w.cs_w = reinterpret_cast<float*>(b + o_csw);
     w.topk_idx = reinterpret_cast<int32_t*>(b + o_tidx);
     w.topk_w = reinterpret_cast<float*>(b + o_tw);
     w.sgate = reinterpret_cast<float*>(b + o_sg);
     w.x_perm = reinterpret_cast<uint16_t*>(b + o_xp);
     w.xsum = reinterpret_cast<float*>(b + o_xs);
-    w.h_hi = reinterpret_cast<uint16_t*>(b + o_hh);
-    w.h_lo = reinterpret_cast<uint16_t*>(b + o_hl);
+    w.h16 = reinterpret_cast<uint16_t*>(b + o_hh);
     w.y_pair = reinterpret_cast<float*>(b + o_y);
+    w.partials = reinterpret_cast<float*>(b + o_part);
+    w.counters = reinterpret_cast<int*>(b + o_cnt);
   }
   return w;
 }

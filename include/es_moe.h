@@ -60,13 +60,15 @@ typedef enum es_dtype {
 #define ES_DEVERR_BAD_EXPERT_ID 0x1u   /* top-k index outside [-1, E)        */
 #define ES_DEVERR_NONFINITE_LOGIT 0x2u /* NaN logit seen by the router        */
 #define ES_DEVERR_CAPACITY 0x4u        /* pair list larger than the workspace */
+#define ES_DEVERR_TIMEOUT 0x8u         /* a bounded in-kernel wait gave up    */
+#define ES_DEVERR_RANGE 0x10u          /* |silu(g)*u| beyond fp16, saturated  */
 
 /* Shape of one MoE block. Mirrors the streaming config.json keys the
  * reference reads (download.py:477-523: num_experts, num_experts_per_tok,
  * moe_intermediate_size, norm_topk_prob, shared_expert_intermediate_size,
  * quantization{bits, group_size}). */
 typedef struct es_moe_cfg {
-  int32_t hidden;         /* D, multiple of 256, <= 4096                       */
+  int32_t hidden;         /* D = 256 * {1,2,3,4,6,8,12,16}                    */
   int32_t num_experts;    /* E routed experts, 1..1024                       */
   int32_t top_k;          /* k, 1..16, k <= E                                 */
   int32_t inter;          /* I: 256, 512, 768, 1024, 1536 or 2048             */
@@ -114,7 +116,9 @@ ES_API es_status es_moe_prepare(const es_moe_cfg* cfg, const es_mlx_layer* layer
                          void* packed, size_t packed_bytes, es_stream_t stream);
 
 /* Workspace bytes needed by es_moe_forward / es_moe_expert_ffn for up to
- * `max_tokens` tokens per call. */
+ * `max_tokens` tokens per call (non-decreasing in max_tokens). The workspace
+ * must be zero-filled once before its first use (it holds counters that the
+ * kernels return to zero after every call). */
 ES_API es_status es_moe_workspace_bytes(const es_moe_cfg* cfg, int32_t max_tokens,
                                  size_t* bytes_out);
 

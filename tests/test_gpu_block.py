@@ -76,17 +76,22 @@ def _check_forward(cfg, T, bias, seed, device, check_bf16=True):
     return err / rms, n_exact, n_tie
 
 
+# The parity bar is 1e-2 x RMS; the kernels land near 1e-3 (h is carried in
+# fp16 into the down projection), which these tighter checks pin.
+KERNEL_REL = 3e-3
+
+
 @pytest.mark.parametrize("T", [1, 5, 33, 100])
 @pytest.mark.parametrize("bias", [False, True])
 def test_small_forward(cuda, T, bias):
     rel, _, _ = _check_forward(SMALL, T, bias, seed=T, device=cuda)
-    assert rel < 1e-4
+    assert rel < KERNEL_REL
 
 
 @pytest.mark.parametrize("T", [1, 17, 70])
 def test_small_shared_expert(cuda, T):
     rel, _, _ = _check_forward(SMALL_SHARED, T, True, seed=3 + T, device=cuda)
-    assert rel < 1e-4
+    assert rel < KERNEL_REL
 
 
 @pytest.mark.parametrize("T", [2, 40])
@@ -186,6 +191,19 @@ def test_nan_logit_is_flagged(cuda):
     _, idx, _ = blk.forward(x, logits, return_routing=True)
     assert blk.read_device_error() & _native.DEVERR_NONFINITE_LOGIT
     assert 5 not in idx[1].tolist()
+
+
+def test_fp16_range_of_h_is_flagged(cuda):
+    """Activations large enough that silu(g)*u leaves the fp16 range: the
+    kernel saturates h and sets ES_DEVERR_RANGE instead of producing inf."""
+    cfg = SMALL
+    lay, _ = _layer(cfg, 7, cuda)
+    x, _, logits, _ = synthetic_inputs(cfg, 2, seed=16, device=cuda)
+    big = (x.float() * 2000.0).to(torch.bfloat16)
+    blk = MoEBlock(cfg, weights=lay, max_tokens=2)
+    out = blk.forward(big, logits, out_dtype=torch.float32)
+    assert blk.read_device_error() & 0x10
+    assert torch.isfinite(out).all()
 
 
 def test_empty_batch(cuda):
