@@ -54,6 +54,7 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--placement", default="hrw", choices=["hrw", "bounded"])
     return ap.parse_args()
 
 
@@ -373,6 +374,127 @@ def run_ours_single(args):
     print(json.dumps(line), flush=True)
 
 
+def run_ours_ep(args):
+    """N GPUs, one process each: the same Qwen3-30B-A3B-shaped layer with its
+    experts sharded by rendezvous hashing over gpu0..gpu{N-1}; every rank
+    keeps a decode batch of --tokens home tokens (weak scaling: N x T tokens
+    per step), NCCL all_gather / all_to_all move activations, masks and fp32
+    partials. Timed with CUDA events, max over ranks."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+    from expert_sniper_b200 import MoEBlock, PRESETS, ep
+    from expert_sniper_b200.quant import cache_bias_vector, synthetic_inputs, synthetic_layer
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", str(rank)))
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    cfg = PRESETS["qwen3-30b-a3b"]
+    T, L = args.tokens, max(2, args.layers)
+    pl = ep.make_placement(cfg.num_experts, world, args.placement)
+    lcfg = cfg.with_(num_experts=max(1, max(pl.counts)))
+    ws = MoEBlock.new_workspace(lcfg, world * T, dev)
+    bias = cache_bias_vector(cfg.num_experts, 0.5, 0)[0].to(dev)
+    backends, xs, lgs, touched = [], [], [], []
+    for l in range(L):
+        lay = synthetic_layer(cfg, seed=1000 + l, device=dev)
+        backends.append(ep.CudaEPBackend(cfg, pl, rank, layer=lay, max_tokens=T, device=dev,
+                                         workspace=ws))
+        del lay
+        x, _, lg, _ = synthetic_inputs(cfg, T, seed=100_000 * rank + l, device=dev)
+        xs.append(x)
+        lgs.append(lg)
+    torch.cuda.empty_cache()
+    # experts this rank reads per layer: owned and chosen by any rank's token
+    for l in range(L):
+        idx, _ = backends[l].route(lgs[l], bias)
+        sel = torch.zeros(cfg.num_experts, dtype=torch.int32, device=dev)
+        sel[idx.long().flatten()] = 1
+        dist.all_reduce(sel, op=dist.ReduceOp.MAX)
+        owned = torch.tensor(pl.owned[rank], dtype=torch.long, device=dev) \
+            if pl.owned[rank] else torch.zeros(0, dtype=torch.long, device=dev)
+        touched.append(int(sel[owned].sum()) if len(pl.owned[rank]) else 0)
+
+    def step(s):
+        return ep.ep_forward(backends[s % L], xs[s % L], lgs[s % L], bias)
+
+    W = max(3, args.warmup)
+    K = args.steps
+    for s in range(W):
+        step(s)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = ClockSampler(local_rank).start() if rank == 0 else None
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0.record()
+    for s in range(W, W + K):
+        step(s)
+    e1.record()
+    e1.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / K], device=dev)
+    clk = clocks.stop() if clocks else None
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    # e2e: host buffers in, host buffer out, through the same public path
+    xs_h = [x.cpu().pin_memory() for x in xs]
+    lg_h = [g.cpu().pin_memory() for g in lgs]
+    out_h = torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory()
+    xd, ld = torch.empty_like(xs[0]), torch.empty_like(lgs[0])
+    K2 = min(K, 500)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0.record()
+    for s in range(K2):
+        xd.copy_(xs_h[s % L], non_blocking=True)
+        ld.copy_(lg_h[s % L], non_blocking=True)
+        o = ep.ep_forward(backends[s % L], xd, ld, bias)
+        out_h.copy_(o, non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / K2], device=dev)
+    dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    per_gpu_bytes = torch.tensor([statistics.mean(touched) * cfg.bytes_per_expert], device=dev)
+    dist.all_reduce(per_gpu_bytes, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        achieved = float(per_gpu_bytes.item()) / (ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": world * T / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u4xbf16->f32",
+            "data": "synthetic (seeded; random-init 4-bit MLX-affine experts)",
+            "config": {"workload": f"{cfg.name} MoE layer decode, {T} home tokens per GPU, "
+                                   f"experts sharded over {world} GPUs ({args.placement}), "
+                                   f"routing bias +0.5, {L} rotating layers",
+                       "model": cfg.name, "tokens_per_gpu": T, "global_batch": world * T,
+                       "parallelism": f"ep{world}", "placement": args.placement,
+                       "experts_per_gpu": pl.counts,
+                       "l2": f"working set {L} layers x {cfg.packed_bytes / world / 1e6:.0f} MB "
+                             "per GPU > L2"},
+            "roofline": {"bound": "hbm", "kernel": "whole step (max over GPUs of expert bytes)",
+                         "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": achieved / peak, "traffic": None},
+            "e2e": {"value": world * T / (float(e2e_ms.item()) * 1e-3), "unit": UNIT,
+                    "h2d_bytes_per_step": T * (cfg.hidden + cfg.num_experts) * 2,
+                    "d2h_bytes_per_step": T * cfg.hidden * 2},
+            "gpu_launches": 7 * K,
+            "clocks": clk,
+            "cpu_baseline": None,
+            "note": "eager launches (NCCL calls are not graph-captured)",
+        }
+        print(json.dumps(line), flush=True)
+    del backends
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def run_reference(args):
     """The reference's algorithm on the host cores: oracle C restatement."""
     rank = int(os.environ.get("RANK", "0"))
@@ -407,8 +529,7 @@ def main():
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.gpus > 1 or world > 1:
-        from expert_sniper_b200 import ep_bench
-        ep_bench.run(args)
+        run_ours_ep(args)
         return
     run_ours_single(args)
 

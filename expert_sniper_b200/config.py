@@ -29,8 +29,8 @@ class MoEConfig:
             raise ValueError("only 4-bit, group-64 MLX affine experts are supported")
         if self.hidden % 64 or self.inter % 64:
             raise ValueError("hidden and inter must be multiples of 64")
-        if not (1 <= self.top_k <= min(16, self.num_experts)):
-            raise ValueError("top_k must be in [1, min(16, num_experts)]")
+        if not 1 <= self.top_k <= 16:
+            raise ValueError("top_k must be in [1, 16]")
         if self.shared_inter and self.shared_inter != self.inter:
             raise ValueError("a shared expert must have the routed experts' inter size")
 

@@ -24,7 +24,7 @@ es_status check_cfg(const es_moe_cfg* c) {
   if (c->inter % 64 || !(kg == 4 || kg == 8 || kg == 12 || kg == 16 || kg == 24 || kg == 32))
     return ES_ERR_UNSUPPORTED;
   if (c->num_experts > es::kMaxExperts) return ES_ERR_UNSUPPORTED;
-  if (c->top_k > es::kMaxTopK || c->top_k > c->num_experts) return ES_ERR_UNSUPPORTED;
+  if (c->top_k > es::kMaxTopK) return ES_ERR_UNSUPPORTED;
   if (c->shared_inter != 0 && c->shared_inter != c->inter) return ES_ERR_UNSUPPORTED;
   return ES_OK;
 }
@@ -187,6 +187,7 @@ es_status es_moe_route(const es_moe_cfg* cfg, const void* logits, int32_t logits
   if (s != ES_OK) return s;
   if (T < 0) return ES_ERR_INVALID_ARG;
   if (logits_dtype != ES_DTYPE_BF16 && logits_dtype != ES_DTYPE_F32) return ES_ERR_UNSUPPORTED;
+  if (cfg->top_k > cfg->num_experts) return ES_ERR_UNSUPPORTED;
   if (T == 0) return ES_OK;
   if (!logits || !topk_idx || !topk_w) return ES_ERR_INVALID_ARG;
   es::RouteArgs r{};
@@ -241,6 +242,7 @@ es_status es_moe_forward_timed(const es_moe_cfg* cfg, const void* x, const void*
   if (s != ES_OK || T == 0) return s;
   if (!logits) return ES_ERR_INVALID_ARG;
   if (logits_dtype != ES_DTYPE_BF16 && logits_dtype != ES_DTYPE_F32) return ES_ERR_UNSUPPORTED;
+  if (cfg->top_k > cfg->num_experts) return ES_ERR_UNSUPPORTED;
   if (events && n_events != 6) return ES_ERR_INVALID_ARG;
   Marks mk;
   mk.ev = events;

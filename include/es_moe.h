@@ -70,7 +70,7 @@ typedef enum es_dtype {
 typedef struct es_moe_cfg {
   int32_t hidden;         /* D = 256 * {1,2,3,4,6,8,12,16}                    */
   int32_t num_experts;    /* E routed experts, 1..1024                       */
-  int32_t top_k;          /* k, 1..16, k <= E                                 */
+  int32_t top_k;          /* k, 1..16 (k <= E for the router)                 */
   int32_t inter;          /* I: 256, 512, 768, 1024, 1536 or 2048             */
   int32_t group_size;     /* must be 64                                       */
   int32_t bits;           /* must be 4                                        */
@@ -183,6 +183,32 @@ ES_API es_status es_moe_forward_timed(const es_moe_cfg* cfg, const void* x,
                                       void* workspace, size_t workspace_bytes,
                                       es_stream_t stream, void* const* events,
                                       int32_t n_events);
+
+/* ---------------------------------------------------------------------------
+ * Expert parallelism (experts sharded over the GPUs of one box)
+ * ------------------------------------------------------------------------- */
+
+/* Routing masks for every destination rank: for d in [0, world), token t,
+ * slot j:  send_idx[d][t][j] = local_id[e] if owner[e] == d else -1 (e =
+ * topk_idx[t][j]), send_w[d][t][j] = topk_w[t][j]. owner / local_id map a
+ * global expert id to its rank and to its index in that rank's shard.
+ * `workspace` (optional, may be NULL) receives ES_DEVERR_BAD_EXPERT_ID.
+ * Counterpart of the partition mask of compute_partial
+ * (src/expert_network/node.py:158-163), computed once on the home rank. */
+ES_API es_status es_ep_mask(const int32_t* topk_idx, const float* topk_w,
+                            const int32_t* owner, const int32_t* local_id,
+                            int32_t num_experts, int32_t top_k, int32_t T,
+                            int32_t world, int32_t* send_idx, float* send_w,
+                            void* workspace, es_stream_t stream);
+
+/* out[t] = sum over r = 0..world-1, in that order, of partials[r][t] (fp32),
+ * plus extra[t] when extra != NULL (e.g. the shared expert), cast to
+ * out_dtype. partials [world][T][D] f32; 16-byte aligned buffers.
+ * Counterpart of the fixed node-order sum of compute_distributed
+ * (src/expert_network/reader.py:278-286). */
+ES_API es_status es_ep_combine(const float* partials, const float* extra,
+                               int32_t world, int32_t T, int32_t D, void* out,
+                               int32_t out_dtype, es_stream_t stream);
 
 /* Synchronously read (and clear when `clear` != 0) the device error word of
  * a workspace. Blocks the host on `stream`. */

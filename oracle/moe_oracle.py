@@ -268,3 +268,20 @@ def combine_nodes(partials) -> np.ndarray:
         p = np.asarray(p, dtype=np.float32)
         total = p.copy() if total is None else total + p
     return total
+
+
+def ep_mask(idx: np.ndarray, w: np.ndarray, owner, local_id, world: int):
+    """Per-destination routing masks: for rank d, slot j of token t keeps the
+    owner-local id of its expert when d owns it, else -1 (the partition mask
+    of compute_partial, node.py:158-163). Returns ([world, T, k] int32,
+    [world, T, k] fp32)."""
+    owner = np.asarray(owner)
+    local_id = np.asarray(local_id)
+    T, k = idx.shape
+    send_idx = np.full((world, T, k), -1, np.int32)
+    for d in range(world):
+        ok = idx >= 0
+        mine = ok & (owner[np.where(ok, idx, 0)] == d)
+        send_idx[d] = np.where(mine, local_id[np.where(ok, idx, 0)], -1)
+    send_w = np.broadcast_to(w.astype(np.float32), (world, T, k)).copy()
+    return send_idx, send_w

@@ -97,4 +97,4 @@ def test_config_validation_in_python():
     with pytest.raises(ValueError):
         MoEConfig(2048, 128, 8, 768, True, shared_inter=512)
     with pytest.raises(ValueError):
-        MoEConfig(2048, 4, 8, 768, True)
+        MoEConfig(2048, 4, 17, 768, True)
