@@ -58,6 +58,8 @@ _SIGNATURES = {
                                             _I32, _P, _SZ, _P, _P, _I32]),
     "es_ep_mask": (ctypes.c_int, [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P]),
     "es_ep_combine": (ctypes.c_int, [_P, _P, _I32, _I32, _I32, _P, _I32, _P]),
+    "es_moe_forward_noalloc": (ctypes.c_int, [_CFG, _P, _P, _I32, _P, _P, _P, _P, _I32, _P, _P,
+                                              _I32, _P]),
     "es_moe_read_error": (ctypes.c_int, [_P, _I32, ctypes.POINTER(ctypes.c_uint32), _P]),
 }
 

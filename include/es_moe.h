@@ -210,6 +210,26 @@ ES_API es_status es_ep_combine(const float* partials, const float* extra,
                                int32_t world, int32_t T, int32_t D, void* out,
                                int32_t out_dtype, es_stream_t stream);
 
+/* es_moe_forward for callers that cannot allocate device memory (a runtime
+ * that owns the whole GPU arena, a plugin whose host forbids outside
+ * allocations, a loop where cudaMalloc's implicit synchronisation is not
+ * allowed). Same arguments minus the workspace: the scratch is a 64 MiB
+ * array built into the library, resident on every device that loads it
+ * until the process exits. A batch whose es_moe_workspace_bytes exceeds
+ * 64 MiB returns ES_ERR_WORKSPACE. The first call on a device resolves the
+ * array's address (make it before any stream capture on that device). All
+ * calls on a device share the array: order them on one stream, since calls
+ * that overlap on the GPU race. Device error flags are not reported here.
+ * No counterpart in the reference (an addition of this library). */
+ES_API es_status es_moe_forward_noalloc(const es_moe_cfg* cfg, const void* x,
+                                        const void* logits, int32_t logits_dtype,
+                                        const float* cache_bias,
+                                        const void* shared_gate_w,
+                                        const void* packed, void* out,
+                                        int32_t out_dtype, int32_t* topk_idx,
+                                        float* topk_w, int32_t T,
+                                        es_stream_t stream);
+
 /* Synchronously read (and clear when `clear` != 0) the device error word of
  * a workspace. Blocks the host on `stream`. */
 ES_API es_status es_moe_read_error(const void* workspace, int32_t clear,
