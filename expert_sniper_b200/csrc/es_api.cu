@@ -88,6 +88,7 @@ es_status run_ffn(const es_moe_cfg* cfg, const Workspace& w, const void* packed,
   f.h16 = w.h16; f.y_pair = w.y_pair; f.err = w.err;
   f.partials = w.partials; f.counters = w.counters; f.item_ctr = w.item_ctr;
   f.split_k = es::ffn_split_k(T, max_active, cfg->hidden, cfg->inter);
+  f.split_k_down = es::ffn_split_k_down(T, max_active, cfg->hidden, cfg->inter);
   if (mk.mark(2, st) != cudaSuccess) return ES_ERR_CUDA;
   if (es::launch_ffn_gateup(f, max_active, st) != cudaSuccess) return ES_ERR_CUDA;
   if (mk.mark(3, st) != cudaSuccess) return ES_ERR_CUDA;

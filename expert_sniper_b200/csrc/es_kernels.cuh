@@ -64,7 +64,8 @@ struct FfnArgs {
   float* partials;          // split-K partial sums (split_k > 1)
   int* counters;            // split-K arrival counters, zero between calls
   int* item_ctr;            // [2] dynamic item counters (gate/up, down)
-  int split_k;
+  int split_k;              // K split of gate/up items
+  int split_k_down;         // K split of down items
 };
 
 struct CombineArgs {
@@ -113,6 +114,7 @@ cudaError_t launch_front(const RouteArgs& r, const DispatchArgs& d, cudaStream_t
 int sm_count();
 // K split of gate/up items for a batch of T tokens (1 above kSplitKMaxTokens)
 int ffn_split_k(int T, int max_active, int D, int I);
+int ffn_split_k_down(int T, int max_active, int D, int I);
 cudaError_t launch_ffn_gateup(const FfnArgs& a, int max_active, cudaStream_t st);
 cudaError_t launch_ffn_down(const FfnArgs& a, int max_active, cudaStream_t st);
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);

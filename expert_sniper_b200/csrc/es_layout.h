@@ -4,10 +4,13 @@
 // Packed layout (one layer, built once by es_moe_prepare):
 //   experts 0..E-1 (then the shared expert, if any), each exactly
 //   3*D*I*9/16 bytes -- the reference's per-expert bytes, no padding.
-//   Inside an expert:
-//     gate/up region: for rb in [0, I/16), G in [0, D/64), proj in {gate, up}:
-//                     one 576-byte tile
-//     down region:    for rb in [0, D/16), G in [0, I/64): one 576-byte tile
+//   Inside an expert (rb = 16-row block):
+//     gate/up region: for each pair of row blocks, G in [0, D/64), the two
+//                     blocks, proj in {gate, up}: one 576-byte tile
+//     down region:    for each quad of row blocks, G in [0, I/64), the four
+//                     blocks: one 576-byte tile
+//   so a warp streaming one (pair or quad, group) run gets all tiles that
+//   share one activation fragment.
 //   A tile covers 16 rows x 64 columns (one quantisation group):
 //     bytes [0, 512)  codes. Lane l = 4*g + c of a warp owns bytes
 //                     [16l, 16l + 16): words 2c and 2c+1 of the group for
@@ -48,11 +51,16 @@ __host__ __device__ inline size_t expert_bytes(int D, int I) {
 __host__ __device__ inline size_t gateup_region_bytes(int D, int I) {
   return (size_t)2 * D * I * 9 / 16;
 }
+// gate/up tiles: pairs of 16-row blocks, then group, then block of the pair,
+// then (gate, up): the 4 tiles of one (pair, group) are contiguous.
 __host__ __device__ inline size_t gateup_tile_off(int GD, int rb, int G, int proj) {
-  return ((size_t)(rb * GD + G) * 2 + proj) * kTileBytes;
+  return ((((size_t)(rb >> 1) * GD + G) * 2 + (rb & 1)) * 2 + proj) * kTileBytes;
 }
+// down tiles: quads of 16-row blocks, then group, then block of the quad:
+// the 4 tiles of one (quad, group) are contiguous.
 __host__ __device__ inline size_t down_tile_off(int D, int I, int rb, int G) {
-  return gateup_region_bytes(D, I) + (size_t)(rb * (I / kGroup) + G) * kTileBytes;
+  return gateup_region_bytes(D, I) +
+         (((size_t)(rb >> 2) * (I / kGroup) + G) * 4 + (rb & 3)) * kTileBytes;
 }
 // position of element d (0..K-1) of a row in fragment order
 __host__ __device__ inline int frag_pos(int d) {
@@ -82,8 +90,8 @@ struct Workspace {
   float* xsum;         // [T][D/64]
   uint16_t* h16;       // [P][I]    fp16 h, fragment order
   float* y_pair;       // [P][D]
-  float* partials;     // [A][I/16][kMaxSplitK][256]  split-K partials (T <= 8)
-  int* counters;       // [A][I/16]  split-K arrivals; zero between calls
+  float* partials;     // split-K partials (T <= 8): [slot][KS][512]
+  int* counters;       // split-K arrivals per slot; zero between calls
   int* ticket;         // front-end CTAs done; zero between calls
   int* item_ctr;       // [2] FFN work counters
   int W, P, kk, E1;
@@ -130,9 +138,13 @@ inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
   // that amount so the size never shrinks as T grows
   const long long Ts = Tm < kSplitKMaxTokens ? Tm : kSplitKMaxTokens;
   const size_t As = (size_t)((Ts * k < E ? Ts * k : E) + (has_shared ? 1 : 0));
-  const size_t part_items = As * (I / 16) * kMaxSplitK;
-  size_t o_part = take(part_items * 256 * 4);
-  size_t o_cnt = take(A * (I / 16) * 4);
+  // split-K slots of gate/up (row pairs) and down (row quads), 2 KB each
+  const size_t gu_slots = As * (I / 32) * kMaxSplitK;
+  const size_t dn_slots = As * (D / 64) * kMaxSplitK;
+  const size_t part_items = gu_slots > dn_slots ? gu_slots : dn_slots;
+  size_t o_part = take(part_items * 512 * 4);
+  const size_t cnt_gu = A * (I / 32), cnt_dn = A * (D / 64);
+  size_t o_cnt = take((cnt_gu > cnt_dn ? cnt_gu : cnt_dn) * 4);
   w.bytes = off;
   w.W = W;
   w.P = P;

@@ -83,8 +83,9 @@ es_status es_moe_forward_noalloc(const es_moe_cfg* cfg, const void* x, const voi
   const long long routed = (long long)T * cfg->top_k < cfg->num_experts
                                ? (long long)T * cfg->top_k
                                : cfg->num_experts;
-  const size_t counter_bytes =
-      (size_t)(routed + (cfg->shared_inter > 0 ? 1 : 0)) * (cfg->inter / 16) * 4;
+  const size_t A = (size_t)(routed + (cfg->shared_inter > 0 ? 1 : 0));
+  const size_t cnt_gu = A * (cfg->inter / 32), cnt_dn = A * (cfg->hidden / 64);
+  const size_t counter_bytes = (cnt_gu > cnt_dn ? cnt_gu : cnt_dn) * 4;
   if (cudaMemsetAsync(w.err, 0, ctl, st) != cudaSuccess ||
       cudaMemsetAsync(w.bitmap, 0, bitmap_bytes, st) != cudaSuccess ||
       cudaMemsetAsync(w.counters, 0, counter_bytes, st) != cudaSuccess)
