@@ -50,7 +50,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--layers", type=int, default=48)
-    ap.add_argument("--sweep", default="1,8", help="extra decode batch sizes to time")
+    ap.add_argument("--sweep", default="1,8", help="extra decode batch sizes to time (\"\" for none)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -137,15 +137,22 @@ def kernel_bytes(cfg, T, U):
     D, I, E, k = cfg.hidden, cfg.inter, cfg.num_experts, cfg.top_k
     P = T * k
     return {
-        "route": T * E * 2 + E * 4 + T * D * 2 * 2 + T * (D // 64) * 4 + T * k * 8,
-        "dispatch": 2 * T * k * 4 + E * 16,
-        "gateup": U * 2 * D * I * 9 // 16 + T * D * 2 + P * I * 4,
-        "down": U * D * I * 9 // 16 + P * I * 4 + P * D * 4,
+        # router + dispatch + operand prep: logits, bias, x in, x_perm + sums out,
+        # routing lists out
+        "front": T * E * 2 + E * 4 + T * D * 2 * 2 + T * (D // 64) * 4 + 3 * T * k * 8 + E * 16,
+        "gap": 0,
+        # packed gate+up tiles of the distinct experts, x_perm in, fp16 h out
+        "gateup": U * 2 * D * I * 9 // 16 + T * D * 2 + P * I * 2,
+        # packed down tiles, fp16 h in, fp32 per-pair rows out
+        "down": U * D * I * 9 // 16 + P * I * 2 + P * D * 4,
+        # per-pair rows in, bf16 out
         "combine": P * D * 4 + T * D * 2 + T * k * 8,
     }
 
 
-KERNELS = ["route", "dispatch", "gateup", "down", "combine"]
+# intervals between the six events es_moe_forward_timed records: the fused
+# front-end kernel, the (empty) gap before the FFN, gate/up, down, combine
+KERNELS = ["front", "gap", "gateup", "down", "combine"]
 
 
 # --------------------------------------------------------------------------- #
@@ -294,8 +301,8 @@ def run_ours_single(args):
         prof = profile_kernels(xs, lgs, outs, min(K, 4 * L))
         kmean = {k: statistics.mean(v for _, v in prof[k]) for k in KERNELS}
         kb = {k: statistics.mean(kernel_bytes(cfg, Tc, U[l])[k] for l, _ in prof[k]) for k in KERNELS}
-        results[Tc] = dict(ms=ms, bytes=mean_bytes, U=statistics.mean(U), kmean=kmean, kb=kb,
-                           clocks=clk, xs=xs, lgs=lgs, outs=outs)
+        results[Tc] = dict(ms=ms, bytes=mean_bytes, U=statistics.mean(U), U_layers=U, kmean=kmean,
+                           kb=kb, clocks=clk, xs=xs, lgs=lgs, outs=outs)
 
     # e2e through the public API with host buffers
     r = results[T]
@@ -329,14 +336,17 @@ def run_ours_single(args):
     if not args.no_cpu_baseline:
         cpu = cpu_baseline(cfg, T, args.cpu_seconds, cpu_layer)
 
-    dom = max(KERNELS, key=lambda k: r["kmean"][k])
+    dom = max([k for k in KERNELS if k != "gap"], key=lambda k: r["kmean"][k])
     achieved = r["kb"][dom] / (r["kmean"][dom] * 1e-3) / 1e9
+    # DRAM traffic of the dominant kernel from one ncu capture (profiles/),
+    # scaled from the captured launch's algorithmic bytes to this run's mean
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
         with open(tp) as f:
-            tj = json.load(f)
-        traffic = tj.get(f"{cfg.name}:T{T}:{dom}")
+            rec = json.load(f).get(f"{cfg.name}:T{T}:{dom}")
+        if rec:
+            traffic = rec["dram_bytes"] * r["kb"][dom] / rec["algorithmic_bytes"]
     line = {
         "metric": METRIC, "value": T / (r["ms"] * 1e-3), "unit": UNIT, "n_gpus": 1,
         "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": r["ms"],
@@ -352,16 +362,18 @@ def run_ours_single(args):
         "block_roofline": {"bound": "hbm", "achieved": r["bytes"] / (r["ms"] * 1e-3) / 1e9,
                            "peak": peak, "unit": "GB/s",
                            "frac": r["bytes"] / (r["ms"] * 1e-3) / 1e9 / peak,
-                           "bytes_per_step": r["bytes"], "mean_distinct_experts": r["U"]},
+                           "bytes_per_step": r["bytes"], "mean_distinct_experts": r["U"],
+                           "distinct_experts_per_layer": r["U_layers"]},
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "algorithmic_bytes_per_launch": r["kb"][dom],
-                     "launch_ms": r["kmean"][dom]},
+                     "traffic": traffic, "traffic_note": "ncu dram read+write of one launch "
+                     "(profiles/traffic.json), scaled by algorithmic bytes to this run's mean",
+                     "algorithmic_bytes_per_launch": r["kb"][dom], "launch_ms": r["kmean"][dom]},
         "kernel_ms": r["kmean"],
         "e2e": {"value": T / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": T * cfg.hidden * 2 + T * cfg.num_experts * 2,
                 "d2h_bytes_per_step": T * cfg.hidden * 2, "ms_per_step": e2e_ms},
-        "gpu_launches": 5 * args.steps,
+        "gpu_launches": 4 * args.steps,  # front, gate/up, down, combine per step
         "clocks": r["clocks"],
         "cpu_baseline": cpu,
         "sweep": [{"tokens": Tc, "ms_per_step": results[Tc]["ms"],
