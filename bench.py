@@ -55,6 +55,12 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--placement", default="hrw", choices=["hrw", "bounded"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="decode: the headline line (it also carries a short prefill "
+                         "measurement); prefill: only the Qwen3-Next layer prefill")
+    ap.add_argument("--prefill-tokens", type=int, default=4096)
+    ap.add_argument("--prefill-steps", type=int, default=50)
+    ap.add_argument("--no-prefill", action="store_true")
     return ap.parse_args()
 
 
@@ -183,6 +189,120 @@ def cpu_baseline(cfg, T, seconds, layer_np=None, seed=0):
     return {"value": T / med, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"{len(times)} calls of one {cfg.name} layer at T={T} "
                       f"(router + experts + combine), median {med * 1e3:.1f} ms/call"}
+
+
+# --------------------------------------------------------------------------- #
+# prefill: Qwen3-Next-80B-A3B layer, T = 4096 (tensor-core path)
+# --------------------------------------------------------------------------- #
+
+PREFILL_METRIC = "MoE-layer prefill tokens/s (Qwen3-Next-80B-A3B-shaped 4-bit layer, shared expert)"
+
+
+def measure_prefill(T, steps, warmup, layers=2):
+    """One step = one MoE-block forward of a Qwen3-Next-shaped layer (E = 512,
+    k = 10, I = 512, shared expert I = 512 with sigmoid gate) over T prompt
+    tokens. Two layers alternate (2 x 908 MB, far above L2), each graph-
+    captured; CUDA events on the launching stream."""
+    import torch
+    from expert_sniper_b200 import MoEBlock, PRESETS
+    from expert_sniper_b200.block import uses_tensor_path
+    from expert_sniper_b200.quant import synthetic_inputs, synthetic_layer
+
+    cfg = PRESETS["qwen3-next-80b-a3b"]
+    dev = torch.device("cuda:0")
+    ws = MoEBlock.new_workspace(cfg, T, dev)
+    blocks, xs, lgs, outs, U = [], [], [], [], []
+    for l in range(layers):
+        lay = synthetic_layer(cfg, seed=2000 + l, device=dev)
+        x, _, lg, sg = synthetic_inputs(cfg, T, seed=3000 + l, device=dev)
+        blk = MoEBlock(cfg, weights=lay, shared_gate_w=sg, max_tokens=T, workspace=ws)
+        del lay
+        idx, _ = blk.route(lg, None)
+        U.append(int(torch.unique(idx).numel()))
+        blocks.append(blk)
+        xs.append(x)
+        lgs.append(lg)
+        outs.append(torch.empty((T, cfg.hidden), dtype=torch.bfloat16, device=dev))
+    torch.cuda.empty_cache()
+    stream = torch.cuda.Stream(dev)
+    events = []
+    for l in range(layers):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        for e in evs:
+            e.record(stream)
+        events.append(evs)
+    graphs, tgraphs = [], []
+    with torch.cuda.stream(stream):
+        for l in range(layers):
+            blocks[l].forward(xs[l], lgs[l], None, out=outs[l])
+        torch.cuda.synchronize()
+        for l in range(layers):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                blocks[l].forward(xs[l], lgs[l], None, out=outs[l])
+            graphs.append(g)
+            g2 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g2, stream=stream):
+                blocks[l].forward_timed(xs[l], lgs[l], None, events[l], outs[l])
+            tgraphs.append(g2)
+        for s_ in range(max(3, warmup)):
+            graphs[s_ % layers].replay()
+        torch.cuda.synchronize()
+        clocks = ClockSampler(0).start()
+        time.sleep(0.3)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for s_ in range(steps):
+            graphs[s_ % layers].replay()
+        e1.record(stream)
+        e1.synchronize()
+        clk = clocks.stop()
+        ms = e0.elapsed_time(e1) / steps
+        kt = {k: [] for k in KERNELS}
+        for rep in range(4):
+            for l in range(layers):
+                tgraphs[l].replay()
+                torch.cuda.synchronize()
+                for i, name in enumerate(KERNELS):
+                    kt[name].append(events[l][i].elapsed_time(events[l][i + 1]))
+    err = blocks[0].read_device_error()
+    del graphs, tgraphs
+    kmean = {k: statistics.mean(v) for k, v in kt.items()}
+    D, I, k = cfg.hidden, cfg.inter, cfg.top_k
+    flops = 2 * T * (k * 3 * D * I + 3 * D * cfg.shared_inter)
+    ffn_flops = {"gateup": 2 * T * (k + 1) * 2 * D * I, "down": 2 * T * (k + 1) * D * I}
+    mean_u = statistics.mean(U)
+    step_bytes = ((mean_u + 1) * cfg.bytes_per_expert + T * cfg.num_experts * 2
+                  + T * D * 2 * 2)
+    peaks = {}
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            peaks = json.load(f)
+    tpeak = float(peaks.get("bf16_tflops", 1590.0))
+    tkind = "measured" if "bf16_tflops" in peaks else "fallback"
+    hbm, hkind = measured_peaks()
+    dom = max(["gateup", "down"], key=lambda n: kmean[n])
+    return {
+        "metric": PREFILL_METRIC, "value": T / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms,
+        "steps": steps, "tokens": T, "kernel_path": "tensor" if uses_tensor_path(cfg, T) else "decode",
+        "config": {"workload": f"{cfg.name} MoE layer prefill, {T} tokens, no routing bias, "
+                               f"{layers} alternating layers of {cfg.packed_bytes / 1e6:.0f} MB",
+                   "model": cfg.name, "hidden": D, "experts": cfg.num_experts, "top_k": k,
+                   "inter": I, "shared_inter": cfg.shared_inter},
+        "tflops": flops / (ms * 1e-3) / 1e12,
+        "roofline": {"bound": "tensor", "kernel": dom,
+                     "achieved": ffn_flops[dom] / (kmean[dom] * 1e-3) / 1e12, "peak": tpeak,
+                     "peak_kind": tkind, "unit": "TFLOP/s",
+                     "frac": ffn_flops[dom] / (kmean[dom] * 1e-3) / 1e12 / tpeak,
+                     "flops_per_launch": ffn_flops[dom], "launch_ms": kmean[dom]},
+        "block_roofline": {"tensor_frac": flops / (ms * 1e-3) / 1e12 / tpeak,
+                           "hbm_frac": step_bytes / (ms * 1e-3) / 1e9 / hbm,
+                           "flops_per_step": flops, "bytes_per_step": step_bytes,
+                           "mean_distinct_experts": mean_u},
+        "kernel_ms": kmean, "clocks": clk, "device_error": err,
+    }
 
 
 # --------------------------------------------------------------------------- #
@@ -383,6 +503,9 @@ def run_ours_single(args):
                    "kernel_ms": results[Tc]["kmean"]} for Tc in sweep],
         "setup_s": setup_s,
     }
+    if not args.no_prefill:
+        line["prefill"] = measure_prefill(args.prefill_tokens, min(args.prefill_steps, 50),
+                                          3)
     print(json.dumps(line), flush=True)
 
 
@@ -543,7 +666,27 @@ def main():
     if args.gpus > 1 or world > 1:
         run_ours_ep(args)
         return
+    if args.workload == "prefill":
+        run_prefill_only(args)
+        return
     run_ours_single(args)
+
+
+def run_prefill_only(args):
+    """--workload prefill: the prefill measurement as its own JSON line."""
+    import torch
+    torch.cuda.set_device(0)
+    r = measure_prefill(args.prefill_tokens, args.prefill_steps, args.warmup)
+    line = {"metric": r["metric"], "value": r["value"], "unit": UNIT, "n_gpus": 1,
+            "steps": args.prefill_steps, "warmup": max(3, args.warmup),
+            "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u4->f16 x f16 -> f32",
+            "data": "synthetic (seeded; random-init 4-bit MLX-affine experts)",
+            "config": r["config"], "roofline": r["roofline"],
+            "block_roofline": r["block_roofline"], "tflops": r["tflops"],
+            "kernel_ms": r["kernel_ms"], "clocks": r["clocks"],
+            "gpu_launches": 5 * args.prefill_steps, "kernel_path": r["kernel_path"]}
+    print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

@@ -78,6 +78,14 @@ def prepare_packed(cfg: MoEConfig, weights: dict, out: torch.Tensor = None) -> t
     return out
 
 
+def uses_tensor_path(cfg: MoEConfig, T: int) -> bool:
+    """Whether a call with T tokens runs the tensor-core (tcgen05) expert
+    kernels: the rule of es_moe_cfg.kernel_path in include/es_moe.h."""
+    if cfg.kernel_path != "auto":
+        return cfg.kernel_path == "tensor"
+    return T >= 64 and T * cfg.top_k >= 16 * cfg.num_experts
+
+
 class MoEBlock:
     """One layer's MoE block with device-resident packed experts.
 

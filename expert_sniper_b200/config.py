@@ -12,6 +12,9 @@ import ctypes
 from dataclasses import dataclass, replace
 
 
+KERNEL_PATHS = {"auto": 0, "decode": 1, "tensor": 2}
+
+
 @dataclass(frozen=True)
 class MoEConfig:
     hidden: int                 # D
@@ -23,6 +26,9 @@ class MoEConfig:
     group_size: int = 64
     bits: int = 4
     name: str = ""
+    # expert-FFN kernels: "auto", "decode" (CUDA-core GEMV) or "tensor"
+    # (tcgen05 grouped GEMM); no counterpart in the reference
+    kernel_path: str = "auto"
 
     def __post_init__(self):
         if self.group_size != 64 or self.bits != 4:
@@ -33,6 +39,8 @@ class MoEConfig:
             raise ValueError("top_k must be in [1, 16]")
         if self.shared_inter and self.shared_inter != self.inter:
             raise ValueError("a shared expert must have the routed experts' inter size")
+        if self.kernel_path not in KERNEL_PATHS:
+            raise ValueError(f"kernel_path must be one of {sorted(KERNEL_PATHS)}")
 
     @property
     def has_shared(self) -> bool:
@@ -57,7 +65,7 @@ class MoEConfig:
     def to_c(self) -> "CMoECfg":
         return CMoECfg(self.hidden, self.num_experts, self.top_k, self.inter,
                        self.group_size, self.bits, int(self.norm_topk_prob),
-                       self.shared_inter)
+                       self.shared_inter, KERNEL_PATHS[self.kernel_path])
 
 
 class CMoECfg(ctypes.Structure):
@@ -65,7 +73,8 @@ class CMoECfg(ctypes.Structure):
     _fields_ = [("hidden", ctypes.c_int32), ("num_experts", ctypes.c_int32),
                 ("top_k", ctypes.c_int32), ("inter", ctypes.c_int32),
                 ("group_size", ctypes.c_int32), ("bits", ctypes.c_int32),
-                ("norm_topk_prob", ctypes.c_int32), ("shared_inter", ctypes.c_int32)]
+                ("norm_topk_prob", ctypes.c_int32), ("shared_inter", ctypes.c_int32),
+                ("kernel_path", ctypes.c_int32)]
 
 
 # Shapes of the model families the reference serves (engine_olmoe.py:53-54,

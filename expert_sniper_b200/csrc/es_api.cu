@@ -26,7 +26,17 @@ es_status check_cfg(const es_moe_cfg* c) {
   if (c->num_experts > es::kMaxExperts) return ES_ERR_UNSUPPORTED;
   if (c->top_k > es::kMaxTopK) return ES_ERR_UNSUPPORTED;
   if (c->shared_inter != 0 && c->shared_inter != c->inter) return ES_ERR_UNSUPPORTED;
+  if (c->kernel_path < 0 || c->kernel_path > 2) return ES_ERR_INVALID_ARG;
   return ES_OK;
+}
+
+// Tensor-core (tcgen05) expert FFN for batches that give each routed expert
+// enough tokens to fill an MMA tile; the register-operand decode kernels
+// otherwise.
+bool use_tensor_cores(const es_moe_cfg* c, int T) {
+  if (c->kernel_path == 1) return false;
+  if (c->kernel_path == 2) return true;
+  return T >= 64 && (long long)T * c->top_k >= 16LL * c->num_experts;
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -72,6 +82,55 @@ es_status run_front(const es_moe_cfg* cfg, const Workspace& w, es::RouteArgs r,
   return cuda_status(mk.mark(1, st));
 }
 
+// Tensor-core path front end: routing with slot counters + scaled fp16
+// activations (one launch), then slot -> pair scatter.
+es_status run_pf_front(const es_moe_cfg* cfg, const Workspace& w, const es::RouteArgs& r, int T,
+                       cudaStream_t st, const Marks& mk) {
+  es::PfFrontArgs d{};
+  d.cs_pos = w.cs_pos; d.cs_w = w.cs_w; d.rank = w.rank;
+  d.cnt = reinterpret_cast<int*>(w.bitmap);  // zero between calls, like the bitmaps
+  d.off_e = w.wpre; d.n_active = w.n_active; d.act_e = w.act_e; d.act_off = w.act_off;
+  d.act_n = w.act_n; d.ticket = w.ticket; d.item_ctr = w.item_ctr;
+  es::PfScatterArgs sc{};
+  sc.cs_pos = w.cs_pos; sc.rank = w.rank; sc.off_e = w.wpre; sc.pair_tok = w.pair_tok;
+  sc.pos_shared = w.pos; sc.T = T; sc.E = cfg->num_experts; sc.k = cfg->top_k;
+  sc.has_shared = cfg->shared_inter > 0;
+  if (mk.mark(0, st) != cudaSuccess) return ES_ERR_CUDA;
+  if (es::launch_pf_front(r, d, st) != cudaSuccess) return ES_ERR_CUDA;
+  if (es::launch_pf_scatter(sc, st) != cudaSuccess) return ES_ERR_CUDA;
+  return cuda_status(mk.mark(1, st));
+}
+
+// Tensor-core path: grouped GEMMs (gate/up, down) and the fp16-row combine.
+es_status run_pf_ffn(const es_moe_cfg* cfg, const Workspace& w, const void* packed, void* out,
+                     int out_f32, int T, cudaStream_t st, const Marks& mk) {
+  const int E1 = cfg->num_experts + (cfg->shared_inter > 0 ? 1 : 0);
+  const long long pairs = (long long)T * w.kk;
+  const long long tiles = pairs / 128 + (pairs < E1 ? pairs : E1);  // >= sum of ceil(n_e / 128)
+  es::PfArgs a{};
+  a.packed = static_cast<const uint8_t*>(packed);
+  a.expert_bytes = es::expert_bytes(cfg->hidden, cfg->inter);
+  a.D = cfg->hidden; a.I = cfg->inter;
+  a.n_active = w.n_active; a.act_e = w.act_e; a.act_off = w.act_off; a.act_n = w.act_n;
+  a.pair_tok = w.pair_tok; a.x16 = w.x_perm; a.xinv = w.xsum; a.h16 = w.h16;
+  a.y16 = reinterpret_cast<uint16_t*>(w.y_pair); a.err = w.err;
+  const long long gu_units = tiles * (cfg->inter / 128), dn_units = tiles * (cfg->hidden / 128);
+  const int gu_max = gu_units > (1 << 30) ? (1 << 30) : (int)gu_units;
+  const int dn_max = dn_units > (1 << 30) ? (1 << 30) : (int)dn_units;
+  if (mk.mark(2, st) != cudaSuccess) return ES_ERR_CUDA;
+  if (es::launch_pf_gateup(a, T, gu_max, st) != cudaSuccess) return ES_ERR_CUDA;
+  if (mk.mark(3, st) != cudaSuccess) return ES_ERR_CUDA;
+  if (es::launch_pf_down(a, (long long)w.P, dn_max, st) != cudaSuccess) return ES_ERR_CUDA;
+  if (mk.mark(4, st) != cudaSuccess) return ES_ERR_CUDA;
+  es::CombineArgs cb{};
+  cb.cs_pos = w.cs_pos; cb.cs_w = w.cs_w; cb.pos_shared = w.pos; cb.sgate = w.sgate;
+  cb.y_pair = w.y_pair; cb.y_f16 = 1;
+  cb.T = T; cb.D = cfg->hidden; cb.k = cfg->top_k; cb.has_shared = cfg->shared_inter > 0;
+  cb.out = out; cb.out_f32 = out_f32;
+  if (es::launch_combine(cb, st) != cudaSuccess) return ES_ERR_CUDA;
+  return cuda_status(mk.mark(5, st));
+}
+
 // Shared tail of es_moe_forward / es_moe_expert_ffn: FFN and combine.
 es_status run_ffn(const es_moe_cfg* cfg, const Workspace& w, const void* packed, void* out,
                   int out_f32, int T, cudaStream_t st, const Marks& mk) {
@@ -95,7 +154,8 @@ es_status run_ffn(const es_moe_cfg* cfg, const Workspace& w, const void* packed,
   if (es::launch_ffn_down(f, max_active, st) != cudaSuccess) return ES_ERR_CUDA;
   if (mk.mark(4, st) != cudaSuccess) return ES_ERR_CUDA;
   es::CombineArgs cb{};
-  cb.cs_pos = w.cs_pos; cb.cs_w = w.cs_w; cb.pos_shared = w.pos; cb.sgate = w.sgate; cb.y_pair = w.y_pair;
+  cb.cs_pos = w.cs_pos; cb.cs_w = w.cs_w; cb.pos_shared = w.pos; cb.sgate = w.sgate;
+  cb.y_pair = w.y_pair; cb.y_f16 = 0;
   cb.T = T; cb.D = cfg->hidden; cb.k = k; cb.has_shared = has_shared;
   cb.out = out; cb.out_f32 = out_f32;
   if (es::launch_combine(cb, st) != cudaSuccess) return ES_ERR_CUDA;
@@ -135,7 +195,7 @@ const char* es_status_str(es_status status) {
   return "unknown status";
 }
 
-int32_t es_version(void) { return (1 << 16) | 0; }
+int32_t es_version(void) { return (1 << 16) | 1; }
 
 es_status es_moe_packed_bytes(const es_moe_cfg* cfg, size_t* bytes_out) {
   es_status s = check_cfg(cfg);
@@ -217,6 +277,12 @@ es_status es_moe_expert_ffn(const es_moe_cfg* cfg, const void* x, const int32_t*
   r.renorm = cfg->norm_topk_prob != 0; r.has_shared = cfg->shared_inter > 0; r.W = w.W;
   r.sgate = w.sgate; r.x_perm = w.x_perm; r.xsum = w.xsum; r.err = w.err;
   Marks mk;
+  if (use_tensor_cores(cfg, T)) {
+    r.out_idx = nullptr; r.out_w = nullptr;
+    es_status s2 = run_pf_front(cfg, w, r, T, st, mk);
+    if (s2 != ES_OK) return s2;
+    return run_pf_ffn(cfg, w, packed, out, out_dtype == ES_DTYPE_F32, T, st, mk);
+  }
   es_status s2 = run_front(cfg, w, r, topk_idx, topk_w, T, st, mk);
   if (s2 != ES_OK) return s2;
   return run_ffn(cfg, w, packed, out, out_dtype == ES_DTYPE_F32, T, st, mk);
@@ -258,6 +324,11 @@ es_status es_moe_forward_timed(const es_moe_cfg* cfg, const void* x, const void*
   r.renorm = cfg->norm_topk_prob != 0; r.has_shared = cfg->shared_inter > 0; r.W = w.W;
   r.out_idx = idx; r.out_w = wts;
   r.sgate = w.sgate; r.x_perm = w.x_perm; r.xsum = w.xsum; r.err = w.err;
+  if (use_tensor_cores(cfg, T)) {
+    es_status s2 = run_pf_front(cfg, w, r, T, st, mk);
+    if (s2 != ES_OK) return s2;
+    return run_pf_ffn(cfg, w, packed, out, out_dtype == ES_DTYPE_F32, T, st, mk);
+  }
   es_status s2 = run_front(cfg, w, r, idx, wts, T, st, mk);
   if (s2 != ES_OK) return s2;
   return run_ffn(cfg, w, packed, out, out_dtype == ES_DTYPE_F32, T, st, mk);

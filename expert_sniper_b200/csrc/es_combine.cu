@@ -1,5 +1,6 @@
 // Combine: out[t] = sum_j w[t,j] * y[t,j] in ascending expert id order, in
-// fp32, then + sgate[t] * y_shared[t]; cast to the output dtype.
+// fp32, then + sgate[t] * y_shared[t]; cast to the output dtype. The
+// per-pair rows y are fp32 (decode kernels) or fp16 (tensor-core path).
 //
 // Restates engine.py:40-41 ((out * top_k_weights[..., None]).sum(axis=-2))
 // and the shared-expert add of generate.py:173-178. It is a gather: each
@@ -14,6 +15,15 @@ namespace {
 
 constexpr int kThreads = 256;
 
+ES_DEV float4 load_row4(const void* y, bool y_f16, size_t off) {
+  if (y_f16) {
+    const uint2 v = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(y) + off);
+    return make_float4(lo_half_f(v.x), hi_half_f(v.x), lo_half_f(v.y), hi_half_f(v.y));
+  }
+  return *reinterpret_cast<const float4*>(static_cast<const float*>(y) + off);
+}
+
+template <bool kYF16>
 __global__ void __launch_bounds__(kThreads) combine_kernel(CombineArgs a) {
   const int t = blockIdx.y;
   const int d = (blockIdx.x * kThreads + threadIdx.x) * 4;
@@ -33,7 +43,7 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(CombineArgs a) {
   float4 ys[kMaxTopK];
 #pragma unroll
   for (int r = 0; r < kMaxTopK; ++r)
-    ys[r] = ps[r] >= 0 ? *reinterpret_cast<const float4*>(a.y_pair + (size_t)ps[r] * a.D + d)
+    ys[r] = ps[r] >= 0 ? load_row4(a.y_pair, kYF16, (size_t)ps[r] * a.D + d)
                        : make_float4(0.f, 0.f, 0.f, 0.f);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
@@ -47,7 +57,7 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(CombineArgs a) {
   if (a.has_shared) {
     const int p = a.pos_shared[t];
     const float sg = a.sgate[t];
-    const float4 y = *reinterpret_cast<const float4*>(a.y_pair + (size_t)p * a.D + d);
+    const float4 y = load_row4(a.y_pair, kYF16, (size_t)p * a.D + d);
     acc.x = fmaf(sg, y.x, acc.x);
     acc.y = fmaf(sg, y.y, acc.y);
     acc.z = fmaf(sg, y.z, acc.z);
@@ -67,7 +77,8 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(CombineArgs a) {
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st) {
   if (a.T <= 0) return cudaSuccess;
   dim3 grid((a.D / 4 + kThreads - 1) / kThreads, a.T);
-  return launch_pdl(combine_kernel, grid, dim3(kThreads), 0, st, a);
+  if (a.y_f16) return launch_pdl(combine_kernel<true>, grid, dim3(kThreads), 0, st, a);
+  return launch_pdl(combine_kernel<false>, grid, dim3(kThreads), 0, st, a);
 }
 
 }  // namespace es

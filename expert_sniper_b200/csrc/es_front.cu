@@ -119,29 +119,6 @@ ES_DEV void dispatch_cta(const DispatchArgs& a, int* s_off) {
   }
 }
 
-// Slot order of one token for the combine: lane j < k holds expert e (or -1)
-// and weight w; writes the token's slots sorted by expert id (masked last),
-// the id in cs_pos (turned into a pair index by the dispatch) and the weight
-// in cs_w.
-ES_DEV void sort_slots_warp(const DispatchArgs& a, int t, int e, float w) {
-  const unsigned full = 0xffffffffu;
-  const int lane = threadIdx.x & 31, k = a.k;
-  const bool valid = lane < k && e >= 0;
-  int rank = 0, nvalid = 0, ninv_before = 0;
-  for (int j2 = 0; j2 < k; ++j2) {
-    const int e2 = __shfl_sync(full, e, j2);
-    const bool v2 = e2 >= 0;
-    nvalid += v2;
-    if (valid && v2 && (e2 < e || (e2 == e && j2 < lane))) ++rank;
-    if (!v2 && j2 < lane) ++ninv_before;
-  }
-  if (lane < k) {
-    const int r = valid ? rank : nvalid + ninv_before;
-    a.cs_pos[(size_t)t * k + r] = valid ? e : -1;
-    a.cs_w[(size_t)t * k + r] = w;
-  }
-}
-
 template <int VPL>
 __global__ void __launch_bounds__(kFrontThreads) front_kernel(RouteArgs r, DispatchArgs d) {
   __shared__ int s_off[kMaxExperts + 2];
@@ -171,7 +148,7 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(RouteArgs r, Dispa
       }
     }
     if (!r.bitmap) continue;  // router only
-    sort_slots_warp(d, t, my_e, my_w);
+    sort_slots_warp(d.cs_pos, d.cs_w, k, t, my_e, my_w);
     const uint32_t bit = 1u << (t & 31);
     if (lane < k && my_e >= 0) atomicOr(&r.bitmap[(size_t)my_e * r.W + (t >> 5)], bit);
     if (r.has_shared) {

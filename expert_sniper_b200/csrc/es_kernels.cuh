@@ -1,6 +1,7 @@
 // Launch arguments and host launchers of the MoE block kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -73,10 +74,54 @@ struct CombineArgs {
   const float* cs_w;        // [T][k]
   const int32_t* pos_shared;  // [T]
   const float* sgate;       // [T]
-  const float* y_pair;      // [P][D]
+  const void* y_pair;       // [P][D] fp32, or fp16 when y_f16
+  int y_f16;
   int T, D, k, has_shared;
   void* out;
   int out_f32;
+};
+
+// Tensor-core path (large batches). Front end: routing with per-expert slot
+// counters instead of token bitmaps, scaled fp16 activations in nibble order.
+struct PfFrontArgs {
+  int32_t* cs_pos;          // [T][k] expert id of the r-th smallest id (pair index after scatter)
+  float* cs_w;              // [T][k]
+  int32_t* rank;            // [T][k] rank of the slot inside its expert's list
+  int* cnt;                 // [E] slot counters (zero between calls)
+  int32_t* off_e;           // [E1] first pair of each expert
+  int32_t* n_active;
+  int32_t* act_e;
+  int32_t* act_off;
+  int32_t* act_n;
+  int* ticket;              // CTAs done routing (zero between calls)
+  int* item_ctr;            // [2] zeroed for symmetry with the decode front end
+};
+
+struct PfScatterArgs {
+  int32_t* cs_pos;          // [T][k] expert id in, pair index out
+  const int32_t* rank;      // [T][k]
+  const int32_t* off_e;     // [E1]
+  int32_t* pair_tok;        // [P]
+  int32_t* pos_shared;      // [T]
+  int T, E, k, has_shared;
+};
+
+// Grouped GEMM over (active expert, 128-row block, token tile) units.
+struct alignas(64) PfArgs {
+  CUtensorMap tm_b;         // B rows: x16 (gate/up) or h16 (down); set by the launcher
+  const uint8_t* packed;
+  size_t expert_bytes;
+  int D, I;
+  const int32_t* n_active;
+  const int32_t* act_e;
+  const int32_t* act_off;
+  const int32_t* act_n;
+  const int32_t* pair_tok;
+  const uint16_t* x16;      // [T][D] fp16, nibble order, scaled per token
+  const float* xinv;        // [T] inverse scales
+  uint16_t* h16;            // [P][I] fp16, nibble order
+  uint16_t* y16;            // [P][D] fp16
+  uint32_t* err;
 };
 
 struct PrepareArgs {
@@ -118,6 +163,11 @@ int ffn_split_k_down(int T, int max_active, int D, int I);
 cudaError_t launch_ffn_gateup(const FfnArgs& a, int max_active, cudaStream_t st);
 cudaError_t launch_ffn_down(const FfnArgs& a, int max_active, cudaStream_t st);
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);
+// tensor-core path
+cudaError_t launch_pf_front(const RouteArgs& r, const PfFrontArgs& d, cudaStream_t st);
+cudaError_t launch_pf_scatter(const PfScatterArgs& a, cudaStream_t st);
+cudaError_t launch_pf_gateup(const PfArgs& a, long long tokens, int max_units, cudaStream_t st);
+cudaError_t launch_pf_down(const PfArgs& a, long long pairs, int max_units, cudaStream_t st);
 cudaError_t launch_prepare(const PrepareArgs& a, cudaStream_t st);
 
 }  // namespace es

@@ -25,6 +25,11 @@
 // slot in 0..3, element 16q + s + 4*slot at position 4s + slot. A lane that
 // reads chunk q of a group gets its two B-fragment registers for each of the
 // four k-steps as consecutive words.
+//
+// Nibble order (tensor-core path, x16 and h rows): each run of 8 values
+// 8q..8q+7 is stored as 8q + {0, 4, 1, 5, 2, 6, 3, 7} -- the order in which
+// one packed code word converts to four fp16 pairs (nibbles s and s + 4 per
+// pair) -- so weights and activations share one K permutation.
 #pragma once
 
 #include <stddef.h>
@@ -68,6 +73,11 @@ __host__ __device__ inline int frag_pos(int d) {
   return (q << 4) + 4 * (r & 3) + (r >> 2);
 }
 
+// position of element i of a row in nibble order
+__host__ __device__ inline int nib_pos(int i) {
+  return (i & ~7) | (((i & 3) << 1) | ((i >> 2) & 1));
+}
+
 inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 // Device pointers carved from the caller's workspace for a call with T tokens.
@@ -83,13 +93,17 @@ struct Workspace {
   int32_t* pos;        // [T]       pair of the shared expert
   int32_t* cs_pos;     // [T][k]    pairs of a token in expert id order
   float* cs_w;         // [T][k]    their weights
+  int32_t* rank;       // [T][k]    tensor-core path: slot's rank inside its expert
   int32_t* topk_idx;   // [T][k]
   float* topk_w;       // [T][k]
   float* sgate;        // [T]       shared-expert gate
-  uint16_t* x_perm;    // [T][D]    bf16, fragment order
-  float* xsum;         // [T][D/64]
-  uint16_t* h16;       // [P][I]    fp16 h, fragment order
-  float* y_pair;       // [P][D]
+  uint16_t* x_perm;    // [T][D]    bf16, fragment order (decode kernels);
+                       //           tensor-core path: scaled fp16, nibble order
+  float* xsum;         // [T][D/64] (decode kernels); tensor-core path: [T]
+                       //           inverse power-of-two scale of each x16 row
+  uint16_t* h16;       // [P][I]    fp16 h, fragment order (decode) or nibble
+                       //           order (tensor-core path)
+  float* y_pair;       // [P][D]    fp32 (decode); fp16 [P][D] (tensor-core path)
   float* partials;     // split-K partials (T <= 8): [slot][KS][512]
   int* counters;       // split-K arrivals per slot; zero between calls
   int* ticket;         // front-end CTAs done; zero between calls
@@ -125,6 +139,7 @@ inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
   size_t o_pos = take((size_t)Tm * kk * 4);
   size_t o_cspos = take((size_t)Tm * k * 4);
   size_t o_csw = take((size_t)Tm * k * 4);
+  size_t o_rank = take((size_t)Tm * k * 4);
   size_t o_tidx = take((size_t)Tm * k * 4);
   size_t o_tw = take((size_t)Tm * k * 4);
   size_t o_sg = take((size_t)Tm * 4);
@@ -165,6 +180,7 @@ inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
     w.pos = reinterpret_cast<int32_t*>(b + o_pos);
     w.cs_pos = reinterpret_cast<int32_t*>(b + o_cspos);
     w.cs_w = reinterpret_cast<float*>(b + o_csw);
+    w.rank = reinterpret_cast<int32_t*>(b + o_rank);
     w.topk_idx = reinterpret_cast<int32_t*>(b + o_tidx);
     w.topk_w = reinterpret_cast<float*>(b + o_tw);
     w.sgate = reinterpret_cast<float*>(b + o_sg);

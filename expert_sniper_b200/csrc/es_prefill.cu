@@ -1,0 +1,810 @@
+// Tensor-core path of the MoE block for large batches (prefill): the expert
+// FFN as a grouped GEMM on the 5th-generation tensor cores (tcgen05.mma,
+// accumulators in tensor memory), with the 4-bit weights dequantised to fp16
+// in shared memory on the way.
+//
+// Restates the same math as the decode kernels (engine.py:32-41 gather_qmm
+// gate/up, SwiGLU, gather_qmm down; generate.py:173-178 shared expert), for
+// batches where each expert sees many tokens, so weights are read once per
+// 128-token tile instead of once per few tokens.
+//
+// Kernels, in launch order (one stream, programmatic dependent launches):
+//   pf_front    router (generate.py:122-136) per token; per-expert slot
+//               counters (atomicAdd -- the rank inside an expert's list is
+//               arbitrary, which changes where a pair's rows live but not any
+//               value: every GEMM column and the combine's expert-id-ordered
+//               sum are independent of it); activations to fp16 with a
+//               per-token power-of-two scale, in nibble order. The last CTA
+//               scans the counts into expert offsets and the active list.
+//   pf_scatter  slot -> pair index, pair -> token.
+//   pf_gemm<1>  gate/up: per unit (expert, 128 rows of I, <=128 tokens) two
+//               accumulators [128 x N] in TMEM; epilogue SwiGLU -> fp16 h.
+//   pf_gemm<0>  down: per unit (expert, 128 rows of D, <=128 tokens) one
+//               accumulator; epilogue -> fp16 per-pair rows (saturated
+//               and flagged beyond the fp16 range, as h is).
+//   combine     (es_combine.cu) fixed expert-id order, fp32.
+//
+// GEMM orientation: A = weights (M = 128 rows, K-major, dequantised into a
+// 128-byte-swizzled smem tile), B = activations of the unit's tokens
+// (N = tokens rounded up to 16, K-major, gathered rows), D = A * B^T in TMEM
+// (lane = weight row, column = token). Weights are the large operand and are
+// read from HBM exactly once per token tile.
+//
+// Warp roles of the persistent CTA (16 warps, one CTA per SM):
+//   warp 0      bulk-copies the packed code tiles of each K-block (64 columns,
+//               one quantisation group) into a ring (raw_full / raw_empty)
+//   warp 1      allocates TMEM; one lane issues tcgen05.mma and commits
+//   warp 2      loads the B rows by TMA into their ring: gate/up gathers
+//               token rows of x16 (tile::gather4, four one-row boxes per
+//               instruction), down copies 128 consecutive pair rows of h16
+//   warps 4-7   epilogue: tcgen05.ld from TMEM, math, global stores
+//   warps 8-15  dequantise codes -> fp16 A tiles in the operand ring
+// Every wait is bounded (ES_DEVERR_TIMEOUT); on a timeout each role stops,
+// copies in flight are waited for, and TMEM is freed before returning.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "es_common.cuh"
+#include "es_kernels.cuh"
+#include "es_route.cuh"
+
+namespace es {
+namespace {
+
+// ---------------------------------------------------------------------------
+// tcgen05 / async-copy primitives
+// ---------------------------------------------------------------------------
+ES_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+ES_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+ES_DEV void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                   smem_addr(dst)),
+               "r"(ncols)
+               : "memory");
+}
+ES_DEV void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+ES_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, fp16 inputs, fp32 accumulate
+ES_DEV void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                     uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// mbarrier arrives once every tcgen05 op issued so far by this thread is done
+ES_DEV void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+          smem_addr(bar))
+      : "memory");
+}
+
+// 32 TMEM lanes x 16 consecutive 32-bit columns: thread i of the warp gets
+// lane (base lane + i), columns col .. col + 15
+ES_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+// waits for this thread's tcgen05.ld; the registers pass through an empty
+// volatile asm after the wait so no use of them is scheduled before it
+ES_DEV void tmem_wait_ld(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) opaque(r[i]);
+}
+
+ES_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// generic-proxy writes to shared memory -> visible to the tensor core's reads
+ES_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major rows of 128 bytes (64 fp16),
+// 128-byte swizzle (16-byte chunk c of row r stored at chunk c ^ (r & 7)),
+// 8-row groups 1024 bytes apart. The tile base is 1024-byte aligned.
+ES_DEV uint64_t sw128_desc(const void* p) {
+  const uint32_t a = smem_addr(p);
+  return (uint64_t)((a & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor: fp16 A and B (K-major), fp32 D, M = 128, N = n.
+ES_DEV uint32_t idesc_f16_m128(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// Dequantisation of one packed word (8 codes of one row) to fp16 in nibble
+// order: (q0,q4) (q1,q5) (q2,q6) (q3,q7) as four half2, w = scale * q + bias.
+// 0x6400 | q is exactly 1024 + q in fp16, so the subtraction is exact and the
+// fused multiply-add rounds once.
+// ---------------------------------------------------------------------------
+ES_DEV uint32_t nib_or(uint32_t w) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(r) : "r"(w), "r"(0x000F000Fu), "r"(0x64006400u));
+  return r;
+}
+ES_DEV uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+ES_DEV __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+ES_DEV uint4 dequant_word(uint32_t w, __half2 s2, __half2 b2) {
+  const __half2 k1024 = bits_h2(0x64006400u);
+  uint4 o;
+  o.x = h2_bits(__hfma2(__hsub2(bits_h2(nib_or(w)), k1024), s2, b2));
+  o.y = h2_bits(__hfma2(__hsub2(bits_h2(nib_or(w >> 4)), k1024), s2, b2));
+  o.z = h2_bits(__hfma2(__hsub2(bits_h2(nib_or(w >> 8)), k1024), s2, b2));
+  o.w = h2_bits(__hfma2(__hsub2(bits_h2(nib_or(w >> 12)), k1024), s2, b2));
+  return o;
+}
+
+ES_DEV void st_shared16(void* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
+
+// ---------------------------------------------------------------------------
+// Front end
+// ---------------------------------------------------------------------------
+constexpr int kFrontWarps = 16;
+constexpr int kFrontThreads = kFrontWarps * 32;
+
+// x row (bf16) -> fp16 in nibble order, scaled by 2^s so that the row's
+// largest magnitude lies in [2^14, 2^15): no overflow, and fp16's 11-bit
+// significand holds every bf16 value of the row exactly down to 2^-28 of the
+// maximum. inv = 2^-s is undone exactly on the fp32 accumulators. Rows with
+// a non-finite maximum keep s = 0 (NaN / inf propagate as in the reference).
+ES_DEV void x_row_to_f16(const uint16_t* xr, uint16_t* outr, float* inv_out, int D) {
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const uint4* x4 = reinterpret_cast<const uint4*>(xr);
+  float m = 0.f;
+  for (int c = lane; c < D / 8; c += 32) {
+    const uint4 v = x4[c];
+    const uint32_t ws[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      m = fmaxf(m, fabsf(__uint_as_float(ws[i] << 16)));
+      m = fmaxf(m, fabsf(__uint_as_float(ws[i] & 0xffff0000u)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(full, m, o));
+  int s = 0;
+  if (m > 0.f && m <= 3.4e38f) {
+    const int e = (int)((__float_as_uint(m) >> 23) & 0xffu) - 127;
+    s = 14 - e;
+    s = s < -100 ? -100 : (s > 100 ? 100 : s);
+  }
+  const float scale = __uint_as_float((uint32_t)(127 + s) << 23);
+  if (lane == 0) *inv_out = __uint_as_float((uint32_t)(127 - s) << 23);
+  uint4* o4 = reinterpret_cast<uint4*>(outr);
+  for (int c = lane; c < D / 8; c += 32) {
+    const uint4 v = x4[c];
+    // elements e0..e7: v.x = (e0, e1), v.y = (e2, e3), v.z = (e4, e5), v.w = (e6, e7)
+    const float e0 = __uint_as_float(v.x << 16) * scale, e1 = __uint_as_float(v.x & 0xffff0000u) * scale;
+    const float e2 = __uint_as_float(v.y << 16) * scale, e3 = __uint_as_float(v.y & 0xffff0000u) * scale;
+    const float e4 = __uint_as_float(v.z << 16) * scale, e5 = __uint_as_float(v.z & 0xffff0000u) * scale;
+    const float e6 = __uint_as_float(v.w << 16) * scale, e7 = __uint_as_float(v.w & 0xffff0000u) * scale;
+    uint4 o;
+    o.x = h2_bits(__floats2half2_rn(e0, e4));
+    o.y = h2_bits(__floats2half2_rn(e1, e5));
+    o.z = h2_bits(__floats2half2_rn(e2, e6));
+    o.w = h2_bits(__floats2half2_rn(e3, e7));
+    o4[c] = o;
+  }
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(kFrontThreads) pf_front_kernel(RouteArgs r, PfFrontArgs d) {
+  __shared__ int s_off[kMaxExperts + 2];
+  __shared__ int s_wc[kFrontWarps];
+  __shared__ int s_wf[kFrontWarps];
+  __shared__ int s_last;
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, tid = threadIdx.x;
+  const int E = r.E, k = r.k;
+  pdl_wait();
+  pdl_trigger();
+
+  for (int t = blockIdx.x * kFrontWarps + warp; t < r.T; t += gridDim.x * kFrontWarps) {
+    int my_e = -1;
+    float my_w = 0.f;
+    if (r.logits) {
+      route_token_warp<VPL>(r.logits, r.logits_f32, r.bias, t, E, k, r.renorm, r.err, my_e, my_w);
+      if (lane < k && r.out_idx) {
+        r.out_idx[(size_t)t * k + lane] = my_e;
+        r.out_w[(size_t)t * k + lane] = my_w;
+      }
+    } else if (lane < k) {
+      my_e = r.in_idx[(size_t)t * k + lane];
+      my_w = r.in_w[(size_t)t * k + lane];
+      if (my_e < -1 || my_e >= E) {
+        set_error(r.err, 0x1u);
+        my_e = -1;
+      }
+    }
+    const int pos = sort_slots_warp(d.cs_pos, d.cs_w, k, t, my_e, my_w);
+    if (lane < k && my_e >= 0) d.rank[(size_t)t * k + pos] = atomicAdd(&d.cnt[my_e], 1);
+    if (r.has_shared) {
+      const float gsg = shared_gate_warp(r.x + (size_t)t * r.D, r.sg_w, r.D);
+      if (lane == 0) r.sgate[t] = gsg;
+    }
+    x_row_to_f16(r.x + (size_t)t * r.D, r.x_perm + (size_t)t * r.D, r.xsum + t, r.D);
+  }
+
+  // the last CTA turns the counts into offsets and the active list
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(d.ticket, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int E1 = E + (r.has_shared ? 1 : 0);
+  for (int e = tid; e < E1; e += kFrontThreads) {
+    s_off[e] = e < E ? __ldcg(d.cnt + e) : r.T;
+    if (e < E) d.cnt[e] = 0;
+  }
+  __syncthreads();
+  const int EPT = (E1 + kFrontThreads - 1) / kFrontThreads;
+  const int e_lo = tid * EPT;
+  int vc = 0, vf = 0;
+  for (int q = 0; q < EPT; ++q)
+    if (e_lo + q < E1) { vc += s_off[e_lo + q]; vf += s_off[e_lo + q] > 0; }
+  const int my_c = vc, my_f = vf;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int nc = __shfl_up_sync(full, vc, o);
+    const int nf = __shfl_up_sync(full, vf, o);
+    if (lane >= o) { vc += nc; vf += nf; }
+  }
+  if (lane == 31) { s_wc[warp] = vc; s_wf[warp] = vf; }
+  __syncthreads();
+  if (warp == 0) {
+    int wc = lane < kFrontWarps ? s_wc[lane] : 0, wf = lane < kFrontWarps ? s_wf[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < kFrontWarps; o <<= 1) {
+      const int nc = __shfl_up_sync(full, wc, o);
+      const int nf = __shfl_up_sync(full, wf, o);
+      if (lane >= o) { wc += nc; wf += nf; }
+    }
+    if (lane < kFrontWarps) { s_wc[lane] = wc; s_wf[lane] = wf; }
+  }
+  __syncthreads();
+  int run_c = (warp > 0 ? s_wc[warp - 1] : 0) + vc - my_c;
+  int run_f = (warp > 0 ? s_wf[warp - 1] : 0) + vf - my_f;
+  for (int q = 0; q < EPT; ++q) {
+    const int e = e_lo + q;
+    if (e >= E1) break;
+    const int cnt = s_off[e];
+    d.off_e[e] = run_c;
+    if (cnt > 0) {
+      d.act_e[run_f] = e;
+      d.act_off[run_f] = run_c;
+      d.act_n[run_f] = cnt;
+      ++run_f;
+    }
+    run_c += cnt;
+  }
+  if (tid == 0) {
+    d.n_active[0] = s_wf[kFrontWarps - 1];
+    d.item_ctr[0] = 0;
+    d.item_ctr[1] = 0;
+    *d.ticket = 0;
+  }
+}
+
+__global__ void __launch_bounds__(256) pf_scatter_kernel(PfScatterArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int nk = a.T * a.k;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < nk) {
+    const int e = a.cs_pos[i];
+    if (e >= 0) {
+      const int p = a.off_e[e] + a.rank[i];
+      a.pair_tok[p] = i / a.k;
+      a.cs_pos[i] = p;
+    }
+  } else if (a.has_shared && i < nk + a.T) {
+    const int t = i - nk;
+    const int p = a.off_e[a.E] + t;
+    a.pair_tok[p] = t;
+    a.pos_shared[t] = p;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Grouped GEMM
+// ---------------------------------------------------------------------------
+constexpr int kNT = 128;          // token tile (UMMA N, at most)
+constexpr int kM = 128;           // weight rows per unit (UMMA M)
+constexpr int kThreads = 512;
+constexpr int kWarpLoad = 0, kWarpMma = 1, kWarpB = 2, kWarpEpi0 = 4, kWarpDq0 = 8,
+              kNumDqWarps = 8;
+constexpr int kRun = 4 * kTileBytes;  // four contiguous 576-byte tiles
+
+// Rings: raw code tiles (bulk copies, HBM latency), A = dequantised weights
+// (written by the dequant warps), B = activation rows (TMA, L2 latency).
+template <bool GU>
+struct PfCfg {
+  static constexpr int kProj = GU ? 2 : 1;
+  static constexpr int kTiles = 8 * kProj;  // 16-row tiles per K-block
+  static constexpr int kRawBytes = kTiles * kTileBytes;
+  static constexpr int kABytes = kM * 128;  // one projection
+  static constexpr int kAStage = kProj * kABytes;
+  static constexpr int kBStage = kNT * 128;
+  static constexpr int kRawStages = GU ? 6 : 8;
+  static constexpr int kAStages = GU ? 2 : 3;
+  static constexpr int kBStages = GU ? 6 : 8;
+  static constexpr int kAccCols = kProj * kNT;
+  static constexpr int kTmemCols = 2 * kAccCols;  // two accumulator buffers
+  static constexpr size_t kSmem = 1024 + (size_t)kAStages * kAStage +
+                                  (size_t)kBStages * kBStage + (size_t)kRawStages * kRawBytes;
+};
+
+ES_DEV void tma_gather4(void* dst, const CUtensorMap* tm, int col, int r0, int r1, int r2, int r3,
+                        uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];\n" ::"r"(smem_addr(dst)),
+      "l"(tm), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_addr(bar))
+      : "memory");
+}
+
+ES_DEV void tma_tile2d(void* dst, const CUtensorMap* tm, int col, int row, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];\n" ::"r"(smem_addr(dst)),
+      "l"(tm), "r"(col), "r"(row), "r"(smem_addr(bar))
+      : "memory");
+}
+
+struct Unit {
+  int e, rb, pair0, n;
+};
+
+// unit u -> (expert, row block, token tile); s_ts = tile prefix over the
+// active list (n_act + 1 entries)
+ES_DEV Unit decode_unit(const PfArgs& a, const int* s_ts, int n_act, int RB, int u) {
+  const int t = u / RB;
+  Unit r;
+  r.rb = u - t * RB;
+  int lo = 0, hi = n_act - 1;  // last a with s_ts[a] <= t
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_ts[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  const int ti = t - s_ts[lo];
+  r.e = a.act_e[lo];
+  r.pair0 = a.act_off[lo] + ti * kNT;
+  const int rem = a.act_n[lo] - ti * kNT;
+  r.n = rem < kNT ? rem : kNT;
+  return r;
+}
+
+// waits (bounded) for the last min(q, stages) phases armed on a ring of
+// full barriers: copies still in flight land before the CTA exits
+ES_DEV void drain_ring(uint64_t* full, int stages, int q) {
+  const int first = q > stages ? q - stages : 0;
+  for (int q2 = first; q2 < q; ++q2)
+    if (!mbar_wait_bounded(&full[q2 % stages], (q2 / stages) & 1)) break;
+}
+
+template <bool GU>
+__global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_constant__ PfArgs a) {
+  using C = PfCfg<GU>;
+  extern __shared__ uint8_t dsmem[];
+  __shared__ __align__(8) uint64_t raw_full[C::kRawStages], raw_empty[C::kRawStages];
+  __shared__ __align__(8) uint64_t a_full[C::kAStages], a_empty[C::kAStages];
+  __shared__ __align__(8) uint64_t b_full[C::kBStages], b_empty[C::kBStages];
+  __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], mma_done;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_ts[kMaxExperts + 2];
+  __shared__ int s_wsum[kThreads / 32];
+  __shared__ int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  auto aborted = [&]() { return *reinterpret_cast<volatile int*>(&s_abort) != 0; };
+  auto set_abort = [&]() { *reinterpret_cast<volatile int*>(&s_abort) = 1; };
+  uint8_t* base = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~(uintptr_t)1023);
+  uint8_t* sa = base;
+  uint8_t* sb = sa + (size_t)C::kAStages * C::kAStage;
+  uint8_t* raw = sb + (size_t)C::kBStages * C::kBStage;
+
+  if (tid == 0) {
+    for (int i = 0; i < C::kRawStages; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], kNumDqWarps);
+    }
+    for (int i = 0; i < C::kAStages; ++i) {
+      mbar_init(&a_full[i], kNumDqWarps);
+      mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < C::kBStages; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    mbar_init(&mma_done, 1);
+    s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc(&s_tmem, C::kTmemCols);
+    tmem_relinquish();
+  }
+
+  pdl_wait();
+  // token-tile prefix over the active experts
+  const int n_act = *a.n_active;
+  {
+    const int per = (n_act + kThreads - 1) / kThreads;
+    const int lo = tid * per;
+    int v = 0;
+    for (int q = 0; q < per; ++q)
+      if (lo + q < n_act) v += (a.act_n[lo + q] + kNT - 1) / kNT;
+    const int mine = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int nv = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += nv;
+    }
+    if (lane == 31) s_wsum[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      int w = lane < kThreads / 32 ? s_wsum[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < kThreads / 32; o <<= 1) {
+        const int nw = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += nw;
+      }
+      if (lane < kThreads / 32) s_wsum[lane] = w;
+    }
+    __syncthreads();
+    int run = (warp > 0 ? s_wsum[warp - 1] : 0) + v - mine;
+    for (int q = 0; q < per; ++q) {
+      if (lo + q >= n_act) break;
+      s_ts[lo + q] = run;
+      run += (a.act_n[lo + q] + kNT - 1) / kNT;
+    }
+    if (tid == kThreads - 1) s_ts[n_act] = s_wsum[kThreads / 32 - 1];
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_trigger();
+
+  const uint32_t tmem = s_tmem;
+  const int RB = (GU ? a.I : a.D) / kM;
+  const int KB = (GU ? a.D : a.I) / kGroup;
+  const int units = s_ts[n_act] * RB;
+
+  if (warp == kWarpLoad) {
+    // ---------------- packed code tiles -> raw ring ----------------
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      const int GD = a.D / kGroup;
+      int q = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const Unit un = decode_unit(a, s_ts, n_act, RB, u);
+        const uint8_t* eb = a.packed + (size_t)un.e * a.expert_bytes;
+        for (int kb = 0; kb < KB; ++kb, ++q) {
+          const int s = q % C::kRawStages;
+          if (!mbar_wait_bounded(&raw_empty[s], ((q / C::kRawStages) & 1) ^ 1) || aborted()) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&raw_full[s], C::kRawBytes);
+          uint8_t* dst = raw + (size_t)s * C::kRawBytes;
+#pragma unroll
+          for (int p = 0; p < C::kRawBytes / kRun; ++p) {
+            const size_t off = GU ? gateup_tile_off(GD, 2 * (un.rb * 4 + p), kb, 0)
+                                  : down_tile_off(a.D, a.I, 4 * (un.rb * 2 + p), kb);
+            bulk_copy_g2s(dst + p * kRun, eb + off, kRun, &raw_full[s], pol);
+          }
+        }
+      }
+      if (!ok) { set_error(a.err, 0x8u); set_abort(); }
+      drain_ring(raw_full, C::kRawStages, q);
+    }
+  } else if (warp == kWarpMma) {
+    // ---------------- tensor-core issue ----------------
+    if (lane == 0) {
+      int q = 0, iu = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++iu) {
+        const Unit un = decode_unit(a, s_ts, n_act, RB, u);
+        const uint32_t idesc = idesc_f16_m128((un.n + 15) & ~15);
+        const int buf = iu & 1;
+        if (!mbar_wait_bounded(&acc_empty[buf], ((iu >> 1) & 1) ^ 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d0 = tmem + buf * C::kAccCols;
+        for (int kb = 0; kb < KB; ++kb, ++q) {
+          const int s_a = q % C::kAStages, s_b = q % C::kBStages;
+          if (!mbar_wait_bounded(&a_full[s_a], (q / C::kAStages) & 1) ||
+              !mbar_wait_bounded(&b_full[s_b], (q / C::kBStages) & 1) || aborted()) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* ast = sa + (size_t)s_a * C::kAStage;
+          const uint64_t bdesc = sw128_desc(sb + (size_t)s_b * C::kBStage);
+#pragma unroll
+          for (int pj = 0; pj < C::kProj; ++pj) {
+            const uint64_t adesc = sw128_desc(ast + pj * C::kABytes);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)  // K = 16 per instruction: +32 bytes
+              umma_f16(d0 + pj * kNT, adesc + 2 * kk, bdesc + 2 * kk, idesc,
+                       (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&a_empty[s_a]);
+          umma_commit(&b_empty[s_b]);
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[buf]);
+      }
+      if (!ok) { set_error(a.err, 0x8u); set_abort(); }
+      umma_commit(&mma_done);
+      mbar_wait_bounded(&mma_done, 0);
+    }
+  } else if (warp == kWarpB) {
+    // ---------------- B rows (activations) -> B ring, by TMA ----------------
+    int q = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const Unit un = decode_unit(a, s_ts, n_act, RB, u);
+      const int npad = (un.n + 15) & ~15;
+      int r4[4] = {0, 0, 0, 0};
+      if (GU) {  // token rows 4 lane .. 4 lane + 3 (padding repeats the first token)
+        const int t0 = a.pair_tok[un.pair0];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int j = 4 * lane + i;
+          r4[i] = j < un.n ? a.pair_tok[un.pair0 + j] : t0;
+        }
+      }
+      for (int kb = 0; kb < KB; ++kb, ++q) {
+        const int s = q % C::kBStages;
+        if (!mbar_wait_bounded(&b_empty[s], ((q / C::kBStages) & 1) ^ 1) || aborted()) {
+          ok = false;
+          break;
+        }
+        uint8_t* dst = sb + (size_t)s * C::kBStage;
+        if (GU) {
+          if (lane == 0) mbar_arrive_expect_tx(&b_full[s], (uint32_t)npad * 128u);
+          __syncwarp();
+          if (4 * lane < npad)
+            tma_gather4(dst + 4 * lane * 128, &a.tm_b, kb * kGroup, r4[0], r4[1], r4[2], r4[3],
+                        &b_full[s]);
+        } else if (lane == 0) {
+          mbar_arrive_expect_tx(&b_full[s], (uint32_t)C::kBStage);
+          tma_tile2d(dst, &a.tm_b, kb * kGroup, un.pair0, &b_full[s]);
+        }
+      }
+    }
+    if (!ok && lane == 0) { set_error(a.err, 0x8u); set_abort(); }
+    if (lane == 0) drain_ring(b_full, C::kBStages, q);
+  } else if (warp >= kWarpEpi0 && warp < kWarpEpi0 + 4) {
+    // ---------------- epilogue ----------------
+    const int ew = warp - kWarpEpi0;
+    const int r = 32 * ew + lane;  // weight row inside the unit
+    int iu = 0;
+    bool ok = true;
+    uint32_t range_err = 0;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++iu) {
+      const Unit un = decode_unit(a, s_ts, n_act, RB, u);
+      const int buf = iu & 1;
+      // inverse token scales: lane holds tokens lane + 32 i, shuffled out per column
+      float inv_r[kNT / 32];
+#pragma unroll
+      for (int i = 0; i < kNT / 32; ++i) {
+        const int j = lane + 32 * i;
+        inv_r[i] = (GU && j < un.n) ? a.xinv[a.pair_tok[un.pair0 + j]] : 0.f;
+      }
+      if (!mbar_wait_bounded(&acc_full[buf], (iu >> 1) & 1)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t tb = tmem + ((uint32_t)(32 * ew) << 16) + buf * C::kAccCols;
+      const int npad = (un.n + 15) & ~15;
+      for (int j0 = 0; j0 < npad; j0 += 16) {
+        if (GU) {
+          const int sel = j0 >> 5;
+          const float inv_sel = sel == 0 ? inv_r[0] : sel == 1 ? inv_r[1] : sel == 2 ? inv_r[2] : inv_r[3];
+          uint32_t g[16], v[16];
+          tmem_ld16(tb + j0, g);
+          tmem_ld16(tb + kNT + j0, v);
+          tmem_wait_ld(g);
+          tmem_wait_ld(v);
+          const int col = un.rb * kM + nib_pos(r);
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int j = j0 + jj;
+            const float inv = __shfl_sync(0xffffffffu, inv_sel, (j0 & 31) + jj);
+            if (j < un.n) {
+              const float gg = __uint_as_float(g[jj]) * inv;
+              const float uu = __uint_as_float(v[jj]) * inv;
+              float h = silu_f(gg) * uu;
+              if (fabsf(h) > 65504.f) { range_err = 1; h = copysignf(65504.f, h); }
+              a.h16[(size_t)(un.pair0 + j) * a.I + col] = __half_as_ushort(__float2half_rn(h));
+            }
+          }
+        } else {
+          uint32_t y[16];
+          tmem_ld16(tb + j0, y);
+          tmem_wait_ld(y);
+          const int col = un.rb * kM + r;
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const int j = j0 + jj;
+            if (j < un.n) {
+              float yv = __uint_as_float(y[jj]);
+              if (fabsf(yv) > 65504.f) { range_err = 1; yv = copysignf(65504.f, yv); }
+              a.y16[(size_t)(un.pair0 + j) * a.D + col] = __half_as_ushort(__float2half_rn(yv));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+    if (range_err) set_error(a.err, 0x10u);
+    if (!ok) { if (lane == 0) set_error(a.err, 0x8u); set_abort(); }
+  } else if (warp >= kWarpDq0) {
+    // ---------------- codes -> fp16 A tiles ----------------
+    const int dw = warp - kWarpDq0;  // 16-row block of the unit
+    const int g = lane >> 2, c = lane & 3;
+    int q = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      for (int kb = 0; kb < KB; ++kb, ++q) {
+        const int sr = q % C::kRawStages, s_a = q % C::kAStages;
+        if (!mbar_wait_bounded(&raw_full[sr], (q / C::kRawStages) & 1)) { ok = false; break; }
+        uint4 cw[C::kProj];
+        uint2 sbv[C::kProj];
+#pragma unroll
+        for (int pj = 0; pj < C::kProj; ++pj) {
+          const uint8_t* tile = raw + (size_t)sr * C::kRawBytes + (dw * C::kProj + pj) * kTileBytes;
+          cw[pj] = ld_shared16(tile + 16 * lane);
+          sbv[pj] = ld_shared8(tile + kTileCodeBytes + 8 * g);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[sr]);
+        if (!mbar_wait_bounded(&a_empty[s_a], ((q / C::kAStages) & 1) ^ 1) || aborted()) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int pj = 0; pj < C::kProj; ++pj) {
+          uint8_t* at = sa + (size_t)s_a * C::kAStage + pj * C::kABytes;
+          // rows g and g + 8 of this 16-row block; sbv = (scale, bias) of each
+          const __half2 s_lo = __half2half2(__ushort_as_half((uint16_t)(sbv[pj].x & 0xffffu)));
+          const __half2 b_lo = __half2half2(__ushort_as_half((uint16_t)(sbv[pj].x >> 16)));
+          const __half2 s_hi = __half2half2(__ushort_as_half((uint16_t)(sbv[pj].y & 0xffffu)));
+          const __half2 b_hi = __half2half2(__ushort_as_half((uint16_t)(sbv[pj].y >> 16)));
+          const int row0 = dw * 16 + g, row1 = row0 + 8;
+          // words 2c, 2c+1 of each row: chunks 2c and 2c+1 of the K-block
+          st_shared16(at + row0 * 128 + (((2 * c) ^ g) << 4), dequant_word(cw[pj].x, s_lo, b_lo));
+          st_shared16(at + row0 * 128 + (((2 * c + 1) ^ g) << 4), dequant_word(cw[pj].y, s_lo, b_lo));
+          st_shared16(at + row1 * 128 + (((2 * c) ^ g) << 4), dequant_word(cw[pj].z, s_hi, b_hi));
+          st_shared16(at + row1 * 128 + (((2 * c + 1) ^ g) << 4), dequant_word(cw[pj].w, s_hi, b_hi));
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[s_a]);
+      }
+    }
+    if (!ok) { if (lane == 0) set_error(a.err, 0x8u); set_abort(); }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kWarpMma) tmem_dealloc(tmem, C::kTmemCols);
+}
+
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D fp16 row-major [rows][cols] tensor map, 128-byte swizzle, box of 64
+// columns (one K-block) x box_rows rows
+cudaError_t encode_rows_f16(CUtensorMap* m, const void* base, int cols, long long rows,
+                            int box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kGroup, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <bool GU>
+cudaError_t launch_pf_gemm(const PfArgs& a_in, long long b_rows, int max_units,
+                           cudaStream_t st) {
+  using C = PfCfg<GU>;
+  int grid = sm_count();
+  if (max_units < grid) grid = max_units;
+  if (grid <= 0) return cudaSuccess;
+  PfArgs a = a_in;
+  // gate/up gathers token rows of x16 four at a time (one-row boxes);
+  // down loads 128 consecutive pair rows of h16
+  cudaError_t e = GU ? encode_rows_f16(&a.tm_b, a.x16, a.D, b_rows, 1)
+                     : encode_rows_f16(&a.tm_b, a.h16, a.I, b_rows, kNT);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(pf_gemm_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)C::kSmem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(pf_gemm_kernel<GU>, dim3(grid), dim3(kThreads), C::kSmem, st, a);
+}
+
+template <int VPL>
+cudaError_t launch_pf_front_vpl(const RouteArgs& r, const PfFrontArgs& d, cudaStream_t st) {
+  int blocks = (r.T + kFrontWarps - 1) / kFrontWarps;
+  const int cap = 4 * sm_count();
+  if (blocks > cap) blocks = cap;
+  return launch_pdl(pf_front_kernel<VPL>, dim3(blocks), dim3(kFrontThreads), 0, st, r, d);
+}
+
+}  // namespace
+
+cudaError_t launch_pf_front(const RouteArgs& r, const PfFrontArgs& d, cudaStream_t st) {
+  if (r.T <= 0) return cudaSuccess;
+  const int vpl = (r.E + 31) / 32;
+  if (vpl <= 1) return launch_pf_front_vpl<1>(r, d, st);
+  if (vpl <= 2) return launch_pf_front_vpl<2>(r, d, st);
+  if (vpl <= 4) return launch_pf_front_vpl<4>(r, d, st);
+  if (vpl <= 8) return launch_pf_front_vpl<8>(r, d, st);
+  if (vpl <= 16) return launch_pf_front_vpl<16>(r, d, st);
+  return launch_pf_front_vpl<32>(r, d, st);
+}
+
+cudaError_t launch_pf_scatter(const PfScatterArgs& a, cudaStream_t st) {
+  const int n = a.T * a.k + (a.has_shared ? a.T : 0);
+  if (n <= 0) return cudaSuccess;
+  return launch_pdl(pf_scatter_kernel, dim3((n + 255) / 256), dim3(256), 0, st, a);
+}
+
+cudaError_t launch_pf_gateup(const PfArgs& a, long long tokens, int max_units, cudaStream_t st) {
+  return launch_pf_gemm<true>(a, tokens, max_units, st);
+}
+
+cudaError_t launch_pf_down(const PfArgs& a, long long pairs, int max_units, cudaStream_t st) {
+  return launch_pf_gemm<false>(a, pairs, max_units, st);
+}
+
+}  // namespace es

@@ -118,4 +118,27 @@ ES_DEV float shared_gate_warp(const uint16_t* xrow, const uint16_t* w, int D) {
   return 1.f / (1.f + expf(-dot));
 }
 
+// Slot order of one token for the combine: lane j < k holds expert e (or -1)
+// and weight w; writes the token's slots sorted by expert id (masked last),
+// the id in cs_pos (turned into a pair index by the dispatch) and the weight
+// in cs_w. Returns the lane's slot (-1 for lanes >= k).
+ES_DEV int sort_slots_warp(int32_t* cs_pos, float* cs_w, int k, int t, int e, float w) {
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const bool valid = lane < k && e >= 0;
+  int rank = 0, nvalid = 0, ninv_before = 0;
+  for (int j2 = 0; j2 < k; ++j2) {
+    const int e2 = __shfl_sync(full, e, j2);
+    const bool v2 = e2 >= 0;
+    nvalid += v2;
+    if (valid && v2 && (e2 < e || (e2 == e && j2 < lane))) ++rank;
+    if (!v2 && j2 < lane) ++ninv_before;
+  }
+  if (lane >= k) return -1;
+  const int r = valid ? rank : nvalid + ninv_before;
+  cs_pos[(size_t)t * k + r] = valid ? e : -1;
+  cs_w[(size_t)t * k + r] = w;
+  return r;
+}
+
 }  // namespace es

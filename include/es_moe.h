@@ -76,6 +76,19 @@ typedef struct es_moe_cfg {
   int32_t bits;           /* must be 4                                        */
   int32_t norm_topk_prob; /* 1: renormalise the k selected probabilities      */
   int32_t shared_inter;   /* 0: no shared expert; else its I (must == inter)  */
+  int32_t kernel_path;    /* which expert-FFN kernels run (no reference
+                           * counterpart; results agree within the parity
+                           * tolerance either way):
+                           *   0 = automatic: the tensor-core path when the
+                           *       batch gives the routed experts at least
+                           *       16 (token, expert) pairs each on average
+                           *       (T * top_k >= 16 * num_experts) and
+                           *       T >= 64, the decode path otherwise;
+                           *   1 = decode path (register-operand GEMV on the
+                           *       4-bit codes, fp32 per-pair rows);
+                           *   2 = tensor-core path (tcgen05 grouped GEMM,
+                           *       fp16 operands dequantised in shared
+                           *       memory, fp16 per-pair rows)              */
 } es_moe_cfg;
 
 /* Per-projection MLX tensors for all experts of one layer, stacked on a

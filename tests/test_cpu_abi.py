@@ -65,10 +65,11 @@ def test_workspace_bytes_monotone(lib):
 @pytest.mark.parametrize("bad", [
     dict(group_size=32), dict(bits=8), dict(hidden=2000), dict(hidden=8192), dict(inter=640),
     dict(num_experts=2000), dict(top_k=17), dict(top_k=0), dict(shared_inter=256),
+    dict(kernel_path=3), dict(kernel_path=-1),
 ])
 def test_unsupported_configs_rejected(lib, bad):
     base = dict(hidden=2048, num_experts=128, top_k=8, inter=768, group_size=64, bits=4,
-                norm_topk_prob=1, shared_inter=0)
+                norm_topk_prob=1, shared_inter=0, kernel_path=0)
     base.update(bad)
     c = CMoECfg(**base)
     out = ctypes.c_size_t(0)
@@ -98,3 +99,6 @@ def test_config_validation_in_python():
         MoEConfig(2048, 128, 8, 768, True, shared_inter=512)
     with pytest.raises(ValueError):
         MoEConfig(2048, 4, 17, 768, True)
+    with pytest.raises(ValueError):
+        MoEConfig(2048, 128, 8, 768, True, kernel_path="fast")
+    assert MoEConfig(2048, 128, 8, 768, True, kernel_path="tensor").to_c().kernel_path == 2

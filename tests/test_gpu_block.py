@@ -17,6 +17,7 @@ import torch
 
 from expert_sniper_b200 import MoEBlock, MoEConfig, PRESETS, run_expert_ffn
 from expert_sniper_b200 import _native
+from expert_sniper_b200.block import uses_tensor_path
 from expert_sniper_b200.quant import cache_bias_vector, synthetic_inputs, synthetic_layer
 from oracle import c_oracle as co
 from oracle import moe_oracle as mo
@@ -76,22 +77,29 @@ def _check_forward(cfg, T, bias, seed, device, check_bf16=True):
     return err / rms, n_exact, n_tie
 
 
-# The parity bar is 1e-2 x RMS; the kernels land near 1e-3 (h is carried in
-# fp16 into the down projection), which these tighter checks pin.
+# The parity bar is 1e-2 x RMS; the decode kernels land near 1e-3 (h is
+# carried in fp16 into the down projection), which these tighter checks pin.
+# Batches that select the tensor-core path (fp16 weights, h and y) are held
+# to the level pinned in test_gpu_tensor.py.
 KERNEL_REL = 3e-3
+TENSOR_REL = 6e-3
+
+
+def _rel_bound(cfg, T):
+    return TENSOR_REL if uses_tensor_path(cfg, T) else KERNEL_REL
 
 
 @pytest.mark.parametrize("T", [1, 5, 33, 100])
 @pytest.mark.parametrize("bias", [False, True])
 def test_small_forward(cuda, T, bias):
     rel, _, _ = _check_forward(SMALL, T, bias, seed=T, device=cuda)
-    assert rel < KERNEL_REL
+    assert rel < _rel_bound(SMALL, T)
 
 
 @pytest.mark.parametrize("T", [1, 17, 70])
 def test_small_shared_expert(cuda, T):
     rel, _, _ = _check_forward(SMALL_SHARED, T, True, seed=3 + T, device=cuda)
-    assert rel < KERNEL_REL
+    assert rel < _rel_bound(SMALL_SHARED, T)
 
 
 @pytest.mark.parametrize("T", [2, 40])
