@@ -164,8 +164,21 @@ ES_DEV bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   return ok != 0;
 }
 
+// Non-blocking test of the same condition.
+ES_DEV bool mbar_test_wait(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: gives up after ~2^31 SM cycles (about a second) and reports it.
 ES_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t phase) {
+  if (mbar_test_wait(bar, phase)) return true;  // fast path: no clock read
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, phase)) {
     if (clock64() - t0 > (1LL << 31)) return false;

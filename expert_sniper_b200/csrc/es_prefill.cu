@@ -30,15 +30,18 @@
 // (lane = weight row, column = token). Weights are the large operand and are
 // read from HBM exactly once per token tile.
 //
-// Warp roles of the persistent CTA (16 warps, one CTA per SM):
+// Warp roles of the persistent CTA (24 warps, one CTA per SM):
 //   warp 0      bulk-copies the packed code tiles of each K-block (64 columns,
 //               one quantisation group) into a ring (raw_full / raw_empty)
 //   warp 1      allocates TMEM; one lane issues tcgen05.mma and commits
-//   warp 2      loads the B rows by TMA into their ring: gate/up gathers
-//               token rows of x16 (tile::gather4, four one-row boxes per
-//               instruction), down copies 128 consecutive pair rows of h16
+//   warps 2-3   load the B rows into their ring: gate/up gathers token rows
+//               of x16 with cp.async (completion tracked on the ring's
+//               mbarrier), down copies 128 consecutive pair rows of h16 with
+//               one TMA tile load per K-block
 //   warps 4-7   epilogue: tcgen05.ld from TMEM, math, global stores
-//   warps 8-15  dequantise codes -> fp16 A tiles in the operand ring
+//   warps 8-23  dequantise codes -> fp16 A tiles in their ring: two groups
+//               of eight warps take alternate K-blocks, one 16-row block per
+//               warp
 // Every wait is bounded (ES_DEVERR_TIMEOUT); on a timeout each role stops,
 // copies in flight are waited for, and TMEM is freed before returning.
 #include <cudaTypedefs.h>
@@ -112,6 +115,18 @@ ES_DEV void tmem_wait_ld(uint32_t (&r)[16]) {
 ES_DEV void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
 }
+
+ES_DEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+// the mbarrier's pending count is raised now and lowered when every
+// cp.async issued so far by this thread has landed
+ES_DEV void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];\n" ::"r"(smem_addr(bar))
+               : "memory");
+}
+ES_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
 // generic-proxy writes to shared memory -> visible to the tensor core's reads
 ES_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
@@ -332,13 +347,16 @@ __global__ void __launch_bounds__(256) pf_scatter_kernel(PfScatterArgs a) {
 // ---------------------------------------------------------------------------
 constexpr int kNT = 128;          // token tile (UMMA N, at most)
 constexpr int kM = 128;           // weight rows per unit (UMMA M)
-constexpr int kThreads = 512;
+constexpr int kThreads = 768;
+constexpr int kNumBThreads = 64;  // warps 2-3 (gate/up: cp.async gathers)
 constexpr int kWarpLoad = 0, kWarpMma = 1, kWarpB = 2, kWarpEpi0 = 4, kWarpDq0 = 8,
-              kNumDqWarps = 8;
+              kNumDqWarps = 8,   // one 16-row block each, per K-block
+              kDqGroups = 2;     // groups of kNumDqWarps, alternating K-blocks
 constexpr int kRun = 4 * kTileBytes;  // four contiguous 576-byte tiles
 
-// Rings: raw code tiles (bulk copies, HBM latency), A = dequantised weights
-// (written by the dequant warps), B = activation rows (TMA, L2 latency).
+// Rings: raw code tiles (bulk copies, HBM latency) and operand slots, each
+// holding one K-block of A (dequantised weights, written by the dequant
+// warps) and of B (activation rows), completed on one barrier.
 template <bool GU>
 struct PfCfg {
   static constexpr int kProj = GU ? 2 : 1;
@@ -347,23 +365,13 @@ struct PfCfg {
   static constexpr int kABytes = kM * 128;  // one projection
   static constexpr int kAStage = kProj * kABytes;
   static constexpr int kBStage = kNT * 128;
-  static constexpr int kRawStages = GU ? 6 : 8;
-  static constexpr int kAStages = GU ? 2 : 3;
-  static constexpr int kBStages = GU ? 6 : 8;
+  static constexpr int kRawStages = GU ? 3 : 6;
+  static constexpr int kOpStages = GU ? 4 : 6;  // A and B share slots and barriers
   static constexpr int kAccCols = kProj * kNT;
   static constexpr int kTmemCols = 2 * kAccCols;  // two accumulator buffers
-  static constexpr size_t kSmem = 1024 + (size_t)kAStages * kAStage +
-                                  (size_t)kBStages * kBStage + (size_t)kRawStages * kRawBytes;
+  static constexpr size_t kSmem = 1024 + (size_t)kOpStages * (kAStage + kBStage) +
+                                  (size_t)kRawStages * kRawBytes;
 };
-
-ES_DEV void tma_gather4(void* dst, const CUtensorMap* tm, int col, int r0, int r1, int r2, int r3,
-                        uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];\n" ::"r"(smem_addr(dst)),
-      "l"(tm), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_addr(bar))
-      : "memory");
-}
 
 ES_DEV void tma_tile2d(void* dst, const CUtensorMap* tm, int col, int row, uint64_t* bar) {
   asm volatile(
@@ -376,6 +384,25 @@ ES_DEV void tma_tile2d(void* dst, const CUtensorMap* tm, int col, int row, uint6
 struct Unit {
   int e, rb, pair0, n;
 };
+
+// one lane of the (converged) warp is elected
+ES_DEV bool elect_one() {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(r));
+  return r != 0;
+}
+
+// bounded wait for a converged warp: lane 0 polls the barrier (one poller
+// per warp keeps the barrier unit quiet), the warp barrier then orders the
+// other lanes' accesses after lane 0's acquire
+ES_DEV bool warp_wait(uint64_t* bar, uint32_t phase) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait_bounded(bar, phase);
+  __syncwarp();
+  return __shfl_sync(0xffffffffu, ok, 0);
+}
 
 // unit u -> (expert, row block, token tile); s_ts = tile prefix over the
 // active list (n_act + 1 entries)
@@ -396,12 +423,28 @@ ES_DEV Unit decode_unit(const PfArgs& a, const int* s_ts, int n_act, int RB, int
   return r;
 }
 
+// First timed-out wait of a call: the error word gets ES_DEVERR_TIMEOUT and
+// the next three words (reserved in the workspace's error block) record the
+// wait site (1 loader raw_empty, 2 MMA acc_empty, 3 MMA op_full, 4 / 5 B
+// loader op_empty, 6 epilogue acc_full, 7 / 8 dequant raw_full / op_empty,
+// 9 drain), the CTA and the stage or unit.
+ES_DEV void note_timeout(uint32_t* err, int site, int where) {
+  set_error(err, 0x8u);
+  if (atomicCAS(err + 1, 0u, (uint32_t)site) == 0u) {
+    err[2] = blockIdx.x;
+    err[3] = (uint32_t)where;
+  }
+}
+
 // waits (bounded) for the last min(q, stages) phases armed on a ring of
 // full barriers: copies still in flight land before the CTA exits
-ES_DEV void drain_ring(uint64_t* full, int stages, int q) {
+ES_DEV void drain_ring(uint64_t* full, int stages, int q, uint32_t* err) {
   const int first = q > stages ? q - stages : 0;
   for (int q2 = first; q2 < q; ++q2)
-    if (!mbar_wait_bounded(&full[q2 % stages], (q2 / stages) & 1)) break;
+    if (!mbar_wait_bounded(&full[q2 % stages], (q2 / stages) & 1)) {
+      note_timeout(err, 9, q2);
+      break;
+    }
 }
 
 template <bool GU>
@@ -409,8 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
   using C = PfCfg<GU>;
   extern __shared__ uint8_t dsmem[];
   __shared__ __align__(8) uint64_t raw_full[C::kRawStages], raw_empty[C::kRawStages];
-  __shared__ __align__(8) uint64_t a_full[C::kAStages], a_empty[C::kAStages];
-  __shared__ __align__(8) uint64_t b_full[C::kBStages], b_empty[C::kBStages];
+  __shared__ __align__(8) uint64_t op_full[C::kOpStages], op_empty[C::kOpStages];
   __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], mma_done;
   __shared__ uint32_t s_tmem;
   __shared__ int s_ts[kMaxExperts + 2];
@@ -423,21 +465,19 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
   uint8_t* base = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~(uintptr_t)1023);
   uint8_t* sa = base;
-  uint8_t* sb = sa + (size_t)C::kAStages * C::kAStage;
-  uint8_t* raw = sb + (size_t)C::kBStages * C::kBStage;
+  uint8_t* sb = sa + (size_t)C::kOpStages * C::kAStage;
+  uint8_t* raw = sb + (size_t)C::kOpStages * C::kBStage;
 
   if (tid == 0) {
     for (int i = 0; i < C::kRawStages; ++i) {
       mbar_init(&raw_full[i], 1);
       mbar_init(&raw_empty[i], kNumDqWarps);
     }
-    for (int i = 0; i < C::kAStages; ++i) {
-      mbar_init(&a_full[i], kNumDqWarps);
-      mbar_init(&a_empty[i], 1);
-    }
-    for (int i = 0; i < C::kBStages; ++i) {
-      mbar_init(&b_full[i], 1);
-      mbar_init(&b_empty[i], 1);
+    for (int i = 0; i < C::kOpStages; ++i) {
+      // full: the 8 dequant warps of a K-block plus its B rows (64 cp.async
+      // threads for gate/up, one TMA arrival for down); empty: the MMA commit
+      mbar_init(&op_full[i], kNumDqWarps + (GU ? kNumBThreads : 1));
+      mbar_init(&op_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
@@ -509,10 +549,12 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
         const uint8_t* eb = a.packed + (size_t)un.e * a.expert_bytes;
         for (int kb = 0; kb < KB; ++kb, ++q) {
           const int s = q % C::kRawStages;
-          if (!mbar_wait_bounded(&raw_empty[s], ((q / C::kRawStages) & 1) ^ 1) || aborted()) {
+          if (!mbar_wait_bounded(&raw_empty[s], ((q / C::kRawStages) & 1) ^ 1)) {
+            note_timeout(a.err, 1, q);
             ok = false;
             break;
           }
+          if (aborted()) { ok = false; break; }
           mbar_arrive_expect_tx(&raw_full[s], C::kRawBytes);
           uint8_t* dst = raw + (size_t)s * C::kRawBytes;
 #pragma unroll
@@ -524,85 +566,117 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
         }
       }
       if (!ok) { set_error(a.err, 0x8u); set_abort(); }
-      drain_ring(raw_full, C::kRawStages, q);
+      drain_ring(raw_full, C::kRawStages, q, a.err);
     }
   } else if (warp == kWarpMma) {
     // ---------------- tensor-core issue ----------------
-    if (lane == 0) {
-      int q = 0, iu = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++iu) {
-        const Unit un = decode_unit(a, s_ts, n_act, RB, u);
-        const uint32_t idesc = idesc_f16_m128((un.n + 15) & ~15);
-        const int buf = iu & 1;
-        if (!mbar_wait_bounded(&acc_empty[buf], ((iu >> 1) & 1) ^ 1)) { ok = false; break; }
+    // The whole warp runs the loop (descriptors stay warp-uniform); one
+    // elected lane issues each tcgen05 instruction.
+    int iu = 0, so = 0;
+    uint32_t ph = 0;  // operand ring slot and its phase parity
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++iu) {
+      const Unit un = decode_unit(a, s_ts, n_act, RB, u);
+      const uint32_t idesc = idesc_f16_m128((un.n + 15) & ~15);
+      const int buf = iu & 1;
+      if (!warp_wait(&acc_empty[buf], ((iu >> 1) & 1) ^ 1)) {
+        if (lane == 0) note_timeout(a.err, 2, iu);
+        ok = false;
+        break;
+      }
+      if (aborted()) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d0 = tmem + buf * C::kAccCols;
+      for (int kb = 0; kb < KB; ++kb) {
+        if (!warp_wait(&op_full[so], ph)) {
+          if (lane == 0) note_timeout(a.err, 3, iu * 1024 + kb);
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t d0 = tmem + buf * C::kAccCols;
-        for (int kb = 0; kb < KB; ++kb, ++q) {
-          const int s_a = q % C::kAStages, s_b = q % C::kBStages;
-          if (!mbar_wait_bounded(&a_full[s_a], (q / C::kAStages) & 1) ||
-              !mbar_wait_bounded(&b_full[s_b], (q / C::kBStages) & 1) || aborted()) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint8_t* ast = sa + (size_t)s_a * C::kAStage;
-          const uint64_t bdesc = sw128_desc(sb + (size_t)s_b * C::kBStage);
+        const uint64_t adesc0 = sw128_desc(sa + (size_t)so * C::kAStage);
+        const uint64_t bdesc = sw128_desc(sb + (size_t)so * C::kBStage);
+        if (elect_one()) {
 #pragma unroll
           for (int pj = 0; pj < C::kProj; ++pj) {
-            const uint64_t adesc = sw128_desc(ast + pj * C::kABytes);
+            // projection pj's tile starts kABytes (16 KB = 1024 descriptor units) later
+            const uint64_t adesc = adesc0 + (uint64_t)pj * (C::kABytes >> 4);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)  // K = 16 per instruction: +32 bytes
               umma_f16(d0 + pj * kNT, adesc + 2 * kk, bdesc + 2 * kk, idesc,
                        (kb > 0 || kk > 0) ? 1u : 0u);
           }
-          umma_commit(&a_empty[s_a]);
-          umma_commit(&b_empty[s_b]);
+          umma_commit(&op_empty[so]);
         }
-        if (!ok) break;
-        umma_commit(&acc_full[buf]);
+        __syncwarp();
+        if (++so == C::kOpStages) { so = 0; ph ^= 1u; }
       }
-      if (!ok) { set_error(a.err, 0x8u); set_abort(); }
-      umma_commit(&mma_done);
-      mbar_wait_bounded(&mma_done, 0);
-    }
-  } else if (warp == kWarpB) {
-    // ---------------- B rows (activations) -> B ring, by TMA ----------------
-    int q = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-      const Unit un = decode_unit(a, s_ts, n_act, RB, u);
-      const int npad = (un.n + 15) & ~15;
-      int r4[4] = {0, 0, 0, 0};
-      if (GU) {  // token rows 4 lane .. 4 lane + 3 (padding repeats the first token)
-        const int t0 = a.pair_tok[un.pair0];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int j = 4 * lane + i;
-          r4[i] = j < un.n ? a.pair_tok[un.pair0 + j] : t0;
-        }
-      }
-      for (int kb = 0; kb < KB; ++kb, ++q) {
-        const int s = q % C::kBStages;
-        if (!mbar_wait_bounded(&b_empty[s], ((q / C::kBStages) & 1) ^ 1) || aborted()) {
-          ok = false;
-          break;
-        }
-        uint8_t* dst = sb + (size_t)s * C::kBStage;
-        if (GU) {
-          if (lane == 0) mbar_arrive_expect_tx(&b_full[s], (uint32_t)npad * 128u);
-          __syncwarp();
-          if (4 * lane < npad)
-            tma_gather4(dst + 4 * lane * 128, &a.tm_b, kb * kGroup, r4[0], r4[1], r4[2], r4[3],
-                        &b_full[s]);
-        } else if (lane == 0) {
-          mbar_arrive_expect_tx(&b_full[s], (uint32_t)C::kBStage);
-          tma_tile2d(dst, &a.tm_b, kb * kGroup, un.pair0, &b_full[s]);
-        }
-      }
+      if (!ok) break;
+      if (elect_one()) umma_commit(&acc_full[buf]);
+      __syncwarp();
     }
     if (!ok && lane == 0) { set_error(a.err, 0x8u); set_abort(); }
-    if (lane == 0) drain_ring(b_full, C::kBStages, q);
+    if (elect_one()) umma_commit(&mma_done);
+    __syncwarp();
+    warp_wait(&mma_done, 0);
+  } else if (warp == kWarpB || warp == kWarpB + 1) {
+    // ---------------- B rows (activations) -> B ring ----------------
+    int q = 0;
+    bool ok = true;
+    if (GU) {
+      // token rows of x16, gathered with 16-byte cp.async by 64 threads:
+      // thread bt copies chunk bt % 8 of rows bt / 8 + 8 i; completion is
+      // tracked on the slot's full barrier (cp.async.mbarrier.arrive), so no thread waits on
+      // its copies
+      const int bt = tid - kWarpB * 32, ch = bt & 7, r0 = bt >> 3;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const Unit un = decode_unit(a, s_ts, n_act, RB, u);
+        const uint16_t* rows[kNT / 8];
+#pragma unroll
+        for (int i = 0; i < kNT / 8; ++i) {
+          const int j = r0 + 8 * i;
+          rows[i] = j < un.n ? a.x16 + (size_t)a.pair_tok[un.pair0 + j] * a.D + ch * 8 : nullptr;
+        }
+        for (int kb = 0; kb < KB; ++kb, ++q) {
+          const int s = q % C::kOpStages;
+          if (!warp_wait(&op_empty[s], ((q / C::kOpStages) & 1) ^ 1)) {
+            if (lane == 0) note_timeout(a.err, 4, q);
+            ok = false;
+            break;
+          }
+          if (aborted()) { ok = false; break; }
+          uint8_t* dst = sb + (size_t)s * C::kBStage;
+#pragma unroll
+          for (int i = 0; i < kNT / 8; ++i) {
+            const int j = r0 + 8 * i;
+            if (rows[i]) cp_async16(dst + j * 128 + ((ch ^ (j & 7)) << 4), rows[i] + kb * kGroup);
+          }
+          cp_async_arrive(&op_full[s]);
+          mbar_arrive(&op_full[s]);
+        }
+      }
+      cp_async_wait_all();
+    } else if (warp == kWarpB) {
+      // 128 consecutive pair rows of h16: one TMA tile per K-block
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const Unit un = decode_unit(a, s_ts, n_act, RB, u);
+        for (int kb = 0; kb < KB; ++kb, ++q) {
+          const int s = q % C::kOpStages;
+          if (!warp_wait(&op_empty[s], ((q / C::kOpStages) & 1) ^ 1)) {
+            if (lane == 0) note_timeout(a.err, 5, q);
+            ok = false;
+            break;
+          }
+          if (aborted()) { ok = false; break; }
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&op_full[s], (uint32_t)C::kBStage);
+            tma_tile2d(sb + (size_t)s * C::kBStage, &a.tm_b, kb * kGroup, un.pair0, &op_full[s]);
+          }
+        }
+      }
+      if (lane == 0) drain_ring(op_full, C::kOpStages, q, a.err);
+    }
+    if (!ok && lane == 0) { set_error(a.err, 0x8u); set_abort(); }
   } else if (warp >= kWarpEpi0 && warp < kWarpEpi0 + 4) {
     // ---------------- epilogue ----------------
     const int ew = warp - kWarpEpi0;
@@ -620,7 +694,11 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
         const int j = lane + 32 * i;
         inv_r[i] = (GU && j < un.n) ? a.xinv[a.pair_tok[un.pair0 + j]] : 0.f;
       }
-      if (!mbar_wait_bounded(&acc_full[buf], (iu >> 1) & 1)) { ok = false; break; }
+      if (!warp_wait(&acc_full[buf], (iu >> 1) & 1)) {
+        if (lane == 0) note_timeout(a.err, 6, iu);
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const uint32_t tb = tmem + ((uint32_t)(32 * ew) << 16) + buf * C::kAccCols;
       const int npad = (un.n + 15) & ~15;
@@ -670,14 +748,20 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
     if (!ok) { if (lane == 0) set_error(a.err, 0x8u); set_abort(); }
   } else if (warp >= kWarpDq0) {
     // ---------------- codes -> fp16 A tiles ----------------
-    const int dw = warp - kWarpDq0;  // 16-row block of the unit
+    const int dw = (warp - kWarpDq0) % kNumDqWarps;  // 16-row block of the unit
+    const int grp = (warp - kWarpDq0) / kNumDqWarps;  // takes K-blocks q = grp mod kDqGroups
     const int g = lane >> 2, c = lane & 3;
     int q = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
       for (int kb = 0; kb < KB; ++kb, ++q) {
-        const int sr = q % C::kRawStages, s_a = q % C::kAStages;
-        if (!mbar_wait_bounded(&raw_full[sr], (q / C::kRawStages) & 1)) { ok = false; break; }
+        if (q % kDqGroups != grp) continue;
+        const int sr = q % C::kRawStages, s_a = q % C::kOpStages;
+        if (!warp_wait(&raw_full[sr], (q / C::kRawStages) & 1)) {
+          if (lane == 0) note_timeout(a.err, 7, q);
+          ok = false;
+          break;
+        }
         uint4 cw[C::kProj];
         uint2 sbv[C::kProj];
 #pragma unroll
@@ -688,10 +772,12 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[sr]);
-        if (!mbar_wait_bounded(&a_empty[s_a], ((q / C::kAStages) & 1) ^ 1) || aborted()) {
+        if (!warp_wait(&op_empty[s_a], ((q / C::kOpStages) & 1) ^ 1)) {
+          if (lane == 0) note_timeout(a.err, 8, q);
           ok = false;
           break;
         }
+        if (aborted()) { ok = false; break; }
 #pragma unroll
         for (int pj = 0; pj < C::kProj; ++pj) {
           uint8_t* at = sa + (size_t)s_a * C::kAStage + pj * C::kABytes;
@@ -709,7 +795,7 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
         }
         fence_proxy_async();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[s_a]);
+        if (lane == 0) mbar_arrive(&op_full[s_a]);
       }
     }
     if (!ok) { if (lane == 0) set_error(a.err, 0x8u); set_abort(); }
@@ -761,10 +847,9 @@ cudaError_t launch_pf_gemm(const PfArgs& a_in, long long b_rows, int max_units,
   if (max_units < grid) grid = max_units;
   if (grid <= 0) return cudaSuccess;
   PfArgs a = a_in;
-  // gate/up gathers token rows of x16 four at a time (one-row boxes);
-  // down loads 128 consecutive pair rows of h16
-  cudaError_t e = GU ? encode_rows_f16(&a.tm_b, a.x16, a.D, b_rows, 1)
-                     : encode_rows_f16(&a.tm_b, a.h16, a.I, b_rows, kNT);
+  // down loads 128 consecutive pair rows of h16 per TMA tile; gate/up
+  // gathers token rows with cp.async and needs no tensor map
+  cudaError_t e = GU ? cudaSuccess : encode_rows_f16(&a.tm_b, a.h16, a.I, b_rows, kNT);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(pf_gemm_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)C::kSmem);
