@@ -49,6 +49,8 @@ _SIGNATURES = {
     "es_version": (_I32, []),
     "es_moe_packed_bytes": (ctypes.c_int, [_CFG, ctypes.POINTER(_SZ)]),
     "es_moe_prepare": (ctypes.c_int, [_CFG, ctypes.POINTER(CMlxLayer), _P, _SZ, _P]),
+    "es_moe_prepare_blocks": (ctypes.c_int, [_CFG, _P, _SZ, ctypes.POINTER(ctypes.c_int64),
+                                             ctypes.POINTER(CMlxLayer), _P, _SZ, _P]),
     "es_moe_workspace_bytes": (ctypes.c_int, [_CFG, _I32, ctypes.POINTER(_SZ)]),
     "es_moe_route": (ctypes.c_int, [_CFG, _P, _I32, _P, _I32, _P, _P, _P]),
     "es_moe_expert_ffn": (ctypes.c_int, [_CFG, _P, _P, _P, _P, _P, _P, _I32, _I32, _P, _SZ, _P]),

@@ -81,6 +81,8 @@ def prepare_packed(cfg: MoEConfig, weights: dict, out: torch.Tensor = None) -> t
 def uses_tensor_path(cfg: MoEConfig, T: int) -> bool:
     """Whether a call with T tokens runs the tensor-core (tcgen05) expert
     kernels: the rule of es_moe_cfg.kernel_path in include/es_moe.h."""
+    if cfg.x_dtype == "f16":
+        return True
     if cfg.kernel_path != "auto":
         return cfg.kernel_path == "tensor"
     return T >= 64 and T * cfg.top_k >= 16 * cfg.num_experts
@@ -173,8 +175,9 @@ class MoEBlock:
                 out: torch.Tensor = None):
         cfg = self.cfg
         xf = self._flat(x, cfg.hidden, "x")
-        if xf.dtype != torch.bfloat16:
-            raise ValueError("x must be bf16")
+        want = torch.float16 if cfg.x_dtype == "f16" else torch.bfloat16
+        if xf.dtype != want:
+            raise ValueError(f"x must be {want} (cfg.x_dtype)")
         lg = self._flat(logits, cfg.num_experts, "logits")
         if lg.dtype not in (torch.bfloat16, torch.float32):
             lg = lg.float()
@@ -222,8 +225,9 @@ class MoEBlock:
         """Experts + combine for given routing (-1 ids are skipped)."""
         cfg = self.cfg
         xf = self._flat(x, cfg.hidden, "x")
-        if xf.dtype != torch.bfloat16:
-            raise ValueError("x must be bf16")
+        want = torch.float16 if cfg.x_dtype == "f16" else torch.bfloat16
+        if xf.dtype != want:
+            raise ValueError(f"x must be {want} (cfg.x_dtype)")
         idx = self._flat(topk_idx, cfg.top_k, "topk_idx").to(torch.int32)
         w = self._flat(topk_w, cfg.top_k, "topk_w").to(torch.float32)
         T = xf.shape[0]

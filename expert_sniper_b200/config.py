@@ -13,6 +13,7 @@ from dataclasses import dataclass, replace
 
 
 KERNEL_PATHS = {"auto": 0, "decode": 1, "tensor": 2}
+X_DTYPES = {"bf16": 0, "f16": 1}  # es_dtype codes
 
 
 @dataclass(frozen=True)
@@ -29,6 +30,9 @@ class MoEConfig:
     # expert-FFN kernels: "auto", "decode" (CUDA-core GEMV) or "tensor"
     # (tcgen05 grouped GEMM); no counterpart in the reference
     kernel_path: str = "auto"
+    # activation dtype: "bf16" (the model dtype) or "f16" (the Expert
+    # Network's wire dtype; runs the tensor-core path)
+    x_dtype: str = "bf16"
 
     def __post_init__(self):
         if self.group_size != 64 or self.bits != 4:
@@ -41,6 +45,10 @@ class MoEConfig:
             raise ValueError("a shared expert must have the routed experts' inter size")
         if self.kernel_path not in KERNEL_PATHS:
             raise ValueError(f"kernel_path must be one of {sorted(KERNEL_PATHS)}")
+        if self.x_dtype not in X_DTYPES:
+            raise ValueError(f"x_dtype must be one of {sorted(X_DTYPES)}")
+        if self.x_dtype == "f16" and self.kernel_path == "decode":
+            raise ValueError("the decode kernels read bf16 activations")
 
     @property
     def has_shared(self) -> bool:
@@ -65,7 +73,7 @@ class MoEConfig:
     def to_c(self) -> "CMoECfg":
         return CMoECfg(self.hidden, self.num_experts, self.top_k, self.inter,
                        self.group_size, self.bits, int(self.norm_topk_prob),
-                       self.shared_inter, KERNEL_PATHS[self.kernel_path])
+                       self.shared_inter, KERNEL_PATHS[self.kernel_path], X_DTYPES[self.x_dtype])
 
 
 class CMoECfg(ctypes.Structure):
@@ -74,7 +82,7 @@ class CMoECfg(ctypes.Structure):
                 ("top_k", ctypes.c_int32), ("inter", ctypes.c_int32),
                 ("group_size", ctypes.c_int32), ("bits", ctypes.c_int32),
                 ("norm_topk_prob", ctypes.c_int32), ("shared_inter", ctypes.c_int32),
-                ("kernel_path", ctypes.c_int32)]
+                ("kernel_path", ctypes.c_int32), ("x_dtype", ctypes.c_int32)]
 
 
 # Shapes of the model families the reference serves (engine_olmoe.py:53-54,

@@ -27,6 +27,9 @@ es_status check_cfg(const es_moe_cfg* c) {
   if (c->top_k > es::kMaxTopK) return ES_ERR_UNSUPPORTED;
   if (c->shared_inter != 0 && c->shared_inter != c->inter) return ES_ERR_UNSUPPORTED;
   if (c->kernel_path < 0 || c->kernel_path > 2) return ES_ERR_INVALID_ARG;
+  if (c->x_dtype != ES_DTYPE_BF16 && c->x_dtype != ES_DTYPE_F16) return ES_ERR_UNSUPPORTED;
+  // the decode kernels read bf16 activations only
+  if (c->x_dtype == ES_DTYPE_F16 && c->kernel_path == 1) return ES_ERR_UNSUPPORTED;
   return ES_OK;
 }
 
@@ -34,6 +37,7 @@ es_status check_cfg(const es_moe_cfg* c) {
 // enough tokens to fill an MMA tile; the register-operand decode kernels
 // otherwise.
 bool use_tensor_cores(const es_moe_cfg* c, int T) {
+  if (c->x_dtype == ES_DTYPE_F16) return true;
   if (c->kernel_path == 1) return false;
   if (c->kernel_path == 2) return true;
   return T >= 64 && (long long)T * c->top_k >= 16LL * c->num_experts;
@@ -179,6 +183,22 @@ es_status check_common(const es_moe_cfg* cfg, const void* x, const void* packed,
   return ES_OK;
 }
 
+// Shared tail of es_moe_prepare / es_moe_prepare_blocks: the shared expert
+// (when configured) and the launch.
+es_status prepare_common(const es_moe_cfg* cfg, const es_mlx_layer* layer, es::PrepareArgs& a,
+                         void* packed, es_stream_t stream) {
+  const es_mlx_proj* shared[3] = {&layer->shared_gate_proj, &layer->shared_up_proj,
+                                  &layer->shared_down_proj};
+  const int has_shared = cfg->shared_inter > 0;
+  for (int p = 0; p < 3 && has_shared; ++p) {
+    if (!shared[p]->weight || !shared[p]->scales || !shared[p]->biases) return ES_ERR_INVALID_ARG;
+    a.sw[p] = shared[p]->weight; a.ss[p] = shared[p]->scales; a.sb[p] = shared[p]->biases;
+  }
+  a.D = cfg->hidden; a.I = cfg->inter; a.E = cfg->num_experts; a.has_shared = has_shared;
+  a.packed = static_cast<uint8_t*>(packed);
+  return cuda_status(es::launch_prepare(a, static_cast<cudaStream_t>(stream)));
+}
+
 }  // namespace
 
 extern "C" {
@@ -216,20 +236,54 @@ es_status es_moe_prepare(const es_moe_cfg* cfg, const es_mlx_layer* layer,
   if (packed_bytes < need) return ES_ERR_INVALID_ARG;
   es::PrepareArgs a{};
   const es_mlx_proj* routed[3] = {&layer->gate, &layer->up, &layer->down};
-  const es_mlx_proj* shared[3] = {&layer->shared_gate_proj, &layer->shared_up_proj,
-                                  &layer->shared_down_proj};
-  const int has_shared = cfg->shared_inter > 0;
   for (int p = 0; p < 3; ++p) {
     if (!routed[p]->weight || !routed[p]->scales || !routed[p]->biases) return ES_ERR_INVALID_ARG;
-    a.w[p] = routed[p]->weight; a.s[p] = routed[p]->scales; a.b[p] = routed[p]->biases;
-    if (has_shared) {
-      if (!shared[p]->weight || !shared[p]->scales || !shared[p]->biases) return ES_ERR_INVALID_ARG;
-      a.sw[p] = shared[p]->weight; a.ss[p] = shared[p]->scales; a.sb[p] = shared[p]->biases;
-    }
+    // stacked [E, N, K/8] uint32 and [E, N, K/64] fp16
+    const size_t N = p < 2 ? cfg->inter : cfg->hidden, K = p < 2 ? cfg->hidden : cfg->inter;
+    a.w[p] = reinterpret_cast<const uint8_t*>(routed[p]->weight);
+    a.s[p] = reinterpret_cast<const uint8_t*>(routed[p]->scales);
+    a.b[p] = reinterpret_cast<const uint8_t*>(routed[p]->biases);
+    a.ew[p] = N * (K / 8) * 4;
+    a.es[p] = a.eb[p] = N * (K / es::kGroup) * 2;
   }
-  a.D = cfg->hidden; a.I = cfg->inter; a.E = cfg->num_experts; a.has_shared = has_shared;
-  a.packed = static_cast<uint8_t*>(packed);
-  return cuda_status(es::launch_prepare(a, static_cast<cudaStream_t>(stream)));
+  return prepare_common(cfg, layer, a, packed, stream);
+}
+
+es_status es_moe_prepare_blocks(const es_moe_cfg* cfg, const void* blocks, size_t block_bytes,
+                                const int64_t* inner_offsets, const es_mlx_layer* shared_layer,
+                                void* packed, size_t packed_bytes, es_stream_t stream) {
+  es_status s = check_cfg(cfg);
+  if (s != ES_OK) return s;
+  if (!blocks || !inner_offsets || !packed || !aligned(packed, 256) || !aligned(blocks, 16))
+    return ES_ERR_INVALID_ARG;
+  size_t need = 0;
+  es_moe_packed_bytes(cfg, &need);
+  if (packed_bytes < need) return ES_ERR_INVALID_ARG;
+  const size_t D = cfg->hidden, I = cfg->inter;
+  // per-expert bytes of the 9 tensors in TENSOR_ORDER
+  const size_t nbytes[9] = {I * D / 2, I * (D / 64) * 2, I * (D / 64) * 2,
+                            I * D / 2, I * (D / 64) * 2, I * (D / 64) * 2,
+                            D * I / 2, D * (I / 64) * 2, D * (I / 64) * 2};
+  for (int t = 0; t < 9; ++t) {
+    const int64_t o = inner_offsets[t];
+    if (o < 0 || (size_t)o + nbytes[t] > block_bytes || (o % 4) != 0) return ES_ERR_INVALID_ARG;
+  }
+  if (block_bytes % 16) return ES_ERR_INVALID_ARG;
+  es::PrepareArgs a{};
+  const uint8_t* base = static_cast<const uint8_t*>(blocks);
+  for (int p = 0; p < 3; ++p) {
+    a.w[p] = base + inner_offsets[3 * p];
+    a.s[p] = base + inner_offsets[3 * p + 1];
+    a.b[p] = base + inner_offsets[3 * p + 2];
+    a.ew[p] = a.es[p] = a.eb[p] = block_bytes;
+  }
+  es_mlx_layer lay{};
+  if (shared_layer) {
+    lay.shared_gate_proj = shared_layer->shared_gate_proj;
+    lay.shared_up_proj = shared_layer->shared_up_proj;
+    lay.shared_down_proj = shared_layer->shared_down_proj;
+  }
+  return prepare_common(cfg, &lay, a, packed, stream);
 }
 
 es_status es_moe_workspace_bytes(const es_moe_cfg* cfg, int32_t max_tokens, size_t* bytes_out) {
@@ -275,6 +329,7 @@ es_status es_moe_expert_ffn(const es_moe_cfg* cfg, const void* x, const int32_t*
   r.sg_w = static_cast<const uint16_t*>(shared_gate_w);
   r.T = T; r.D = cfg->hidden; r.E = cfg->num_experts; r.k = cfg->top_k;
   r.renorm = cfg->norm_topk_prob != 0; r.has_shared = cfg->shared_inter > 0; r.W = w.W;
+  r.x_f16 = cfg->x_dtype == ES_DTYPE_F16;
   r.sgate = w.sgate; r.x_perm = w.x_perm; r.xsum = w.xsum; r.err = w.err;
   Marks mk;
   if (use_tensor_cores(cfg, T)) {
@@ -322,6 +377,7 @@ es_status es_moe_forward_timed(const es_moe_cfg* cfg, const void* x, const void*
   r.sg_w = static_cast<const uint16_t*>(shared_gate_w);
   r.T = T; r.D = cfg->hidden; r.E = cfg->num_experts; r.k = cfg->top_k;
   r.renorm = cfg->norm_topk_prob != 0; r.has_shared = cfg->shared_inter > 0; r.W = w.W;
+  r.x_f16 = cfg->x_dtype == ES_DTYPE_F16;
   r.out_idx = idx; r.out_w = wts;
   r.sgate = w.sgate; r.x_perm = w.x_perm; r.xsum = w.xsum; r.err = w.err;
   if (use_tensor_cores(cfg, T)) {

@@ -20,6 +20,7 @@ struct RouteArgs {
   const uint16_t* x;        // [T][D] bf16 or null (route only)
   const uint16_t* sg_w;     // [D] bf16 shared gate weight or null
   int T, D, E, k, renorm, has_shared, W;
+  int x_f16;                // x is fp16 (tensor-core path only), else bf16
   // outputs
   int32_t* out_idx;         // [T][k] or null
   float* out_w;             // [T][k] or null
@@ -125,10 +126,14 @@ struct alignas(64) PfArgs {
 };
 
 struct PrepareArgs {
-  // routed experts, stacked [E, N, K/8] / [E, N, K/64]
-  const uint32_t* w[3];
-  const uint16_t* s[3];
-  const uint16_t* b[3];
+  // routed experts of projection p (gate, up, down): weight / scales / biases
+  // of expert e start at w[p] + e * ew[p] bytes (and likewise s, b), so both
+  // stacked MLX tensors ([E, N, K/8], stride N*K/2 bytes) and the streaming
+  // format's fixed expert blocks (stride = block size) are read in place
+  const uint8_t* w[3];
+  const uint8_t* s[3];
+  const uint8_t* b[3];
+  size_t ew[3], es[3], eb[3];
   // shared expert (no expert axis) or nulls
   const uint32_t* sw[3];
   const uint16_t* ss[3];

@@ -177,12 +177,20 @@ ES_DEV void st_shared16(void* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
 constexpr int kFrontWarps = 16;
 constexpr int kFrontThreads = kFrontWarps * 32;
 
-// x row (bf16) -> fp16 in nibble order, scaled by 2^s so that the row's
-// largest magnitude lies in [2^14, 2^15): no overflow, and fp16's 11-bit
-// significand holds every bf16 value of the row exactly down to 2^-28 of the
-// maximum. inv = 2^-s is undone exactly on the fp32 accumulators. Rows with
-// a non-finite maximum keep s = 0 (NaN / inf propagate as in the reference).
-ES_DEV void x_row_to_f16(const uint16_t* xr, uint16_t* outr, float* inv_out, int D) {
+// x row (bf16, or fp16 with x_f16) -> fp16 in nibble order, scaled by 2^s
+// so that the row's largest magnitude lies in [2^14, 2^15): no overflow, and
+// fp16's 11-bit significand holds every bf16 value of the row exactly down to
+// 2^-28 of the maximum (fp16 input: every value down to 2^-25 of it). inv =
+// 2^-s is undone exactly on the fp32 accumulators. Rows with a non-finite
+// maximum keep s = 0 (NaN / inf propagate as in the reference).
+ES_DEV float x_lo(uint32_t w, bool f16) {
+  return f16 ? __half2float(__ushort_as_half((uint16_t)(w & 0xffffu))) : __uint_as_float(w << 16);
+}
+ES_DEV float x_hi(uint32_t w, bool f16) {
+  return f16 ? __half2float(__ushort_as_half((uint16_t)(w >> 16))) : __uint_as_float(w & 0xffff0000u);
+}
+
+ES_DEV void x_row_to_f16(const uint16_t* xr, uint16_t* outr, float* inv_out, int D, bool f16) {
   const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const uint4* x4 = reinterpret_cast<const uint4*>(xr);
@@ -192,8 +200,8 @@ ES_DEV void x_row_to_f16(const uint16_t* xr, uint16_t* outr, float* inv_out, int
     const uint32_t ws[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      m = fmaxf(m, fabsf(__uint_as_float(ws[i] << 16)));
-      m = fmaxf(m, fabsf(__uint_as_float(ws[i] & 0xffff0000u)));
+      m = fmaxf(m, fabsf(x_lo(ws[i], f16)));
+      m = fmaxf(m, fabsf(x_hi(ws[i], f16)));
     }
   }
 #pragma unroll
@@ -210,10 +218,10 @@ ES_DEV void x_row_to_f16(const uint16_t* xr, uint16_t* outr, float* inv_out, int
   for (int c = lane; c < D / 8; c += 32) {
     const uint4 v = x4[c];
     // elements e0..e7: v.x = (e0, e1), v.y = (e2, e3), v.z = (e4, e5), v.w = (e6, e7)
-    const float e0 = __uint_as_float(v.x << 16) * scale, e1 = __uint_as_float(v.x & 0xffff0000u) * scale;
-    const float e2 = __uint_as_float(v.y << 16) * scale, e3 = __uint_as_float(v.y & 0xffff0000u) * scale;
-    const float e4 = __uint_as_float(v.z << 16) * scale, e5 = __uint_as_float(v.z & 0xffff0000u) * scale;
-    const float e6 = __uint_as_float(v.w << 16) * scale, e7 = __uint_as_float(v.w & 0xffff0000u) * scale;
+    const float e0 = x_lo(v.x, f16) * scale, e1 = x_hi(v.x, f16) * scale;
+    const float e2 = x_lo(v.y, f16) * scale, e3 = x_hi(v.y, f16) * scale;
+    const float e4 = x_lo(v.z, f16) * scale, e5 = x_hi(v.z, f16) * scale;
+    const float e6 = x_lo(v.w, f16) * scale, e7 = x_hi(v.w, f16) * scale;
     uint4 o;
     o.x = h2_bits(__floats2half2_rn(e0, e4));
     o.y = h2_bits(__floats2half2_rn(e1, e5));
@@ -255,10 +263,10 @@ __global__ void __launch_bounds__(kFrontThreads) pf_front_kernel(RouteArgs r, Pf
     const int pos = sort_slots_warp(d.cs_pos, d.cs_w, k, t, my_e, my_w);
     if (lane < k && my_e >= 0) d.rank[(size_t)t * k + pos] = atomicAdd(&d.cnt[my_e], 1);
     if (r.has_shared) {
-      const float gsg = shared_gate_warp(r.x + (size_t)t * r.D, r.sg_w, r.D);
+      const float gsg = shared_gate_warp(r.x + (size_t)t * r.D, r.sg_w, r.D, r.x_f16 != 0);
       if (lane == 0) r.sgate[t] = gsg;
     }
-    x_row_to_f16(r.x + (size_t)t * r.D, r.x_perm + (size_t)t * r.D, r.xsum + t, r.D);
+    x_row_to_f16(r.x + (size_t)t * r.D, r.x_perm + (size_t)t * r.D, r.xsum + t, r.D, r.x_f16 != 0);
   }
 
   // the last CTA turns the counts into offsets and the active list

@@ -2,7 +2,9 @@
 // es_layout.h. Pure byte movement: every code, scale and bias is copied
 // unchanged, so the packed blob has exactly the reference's bytes per expert
 // (3*D*I*9/16). Counterpart of stack_proj (src/mlx_expert_sniper/engine.py:
-// 22-30), which re-stacked the active experts on every call.
+// 22-30), which re-stacked the active experts on every call. The source is
+// either stacked tensors or a streaming-format layer image (fixed-size expert
+// blocks, src/mlx_expert_sniper/download.py:189-248), read in place.
 #include "es_common.cuh"
 #include "es_kernels.cuh"
 
@@ -38,9 +40,12 @@ __global__ void __launch_bounds__(kWarps * 32) prepare_kernel(PrepareArgs a, lon
     dst_off = down_tile_off(D, I, rb, G);
   }
   const bool shared = e >= a.E;
-  const uint32_t* w = shared ? a.sw[proj] : a.w[proj] + (size_t)e * N * (K / 8);
-  const uint16_t* s = shared ? a.ss[proj] : a.s[proj] + (size_t)e * N * (K / kGroup);
-  const uint16_t* b = shared ? a.sb[proj] : a.b[proj] + (size_t)e * N * (K / kGroup);
+  const uint32_t* w = shared ? a.sw[proj]
+                             : reinterpret_cast<const uint32_t*>(a.w[proj] + (size_t)e * a.ew[proj]);
+  const uint16_t* s = shared ? a.ss[proj]
+                             : reinterpret_cast<const uint16_t*>(a.s[proj] + (size_t)e * a.es[proj]);
+  const uint16_t* b = shared ? a.sb[proj]
+                             : reinterpret_cast<const uint16_t*>(a.b[proj] + (size_t)e * a.eb[proj]);
   uint8_t* dst = a.packed + (size_t)e * expert_bytes(D, I) + dst_off;
 
   const int g = lane >> 2, c = lane & 3;

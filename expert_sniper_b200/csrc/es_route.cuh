@@ -101,7 +101,7 @@ ES_DEV float permute_chunk8(const uint16_t* x_row, uint16_t* perm_row, int q8, b
 }
 
 // sigmoid(x . w) of one token, one warp (generate.py:173-178).
-ES_DEV float shared_gate_warp(const uint16_t* xrow, const uint16_t* w, int D) {
+ES_DEV float shared_gate_warp(const uint16_t* xrow, const uint16_t* w, int D, bool x_f16 = false) {
   const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   if (!w) return 1.f;
@@ -110,8 +110,10 @@ ES_DEV float shared_gate_warp(const uint16_t* xrow, const uint16_t* w, int D) {
   float dot = 0.f;
   for (int i = lane; i < D / 2; i += 32) {
     const uint32_t xv = x2[i], wv = w2[i];
-    dot = fmaf(bf16_bits_to_float(xv & 0xffffu), bf16_bits_to_float(wv & 0xffffu), dot);
-    dot = fmaf(bf16_bits_to_float(xv >> 16), bf16_bits_to_float(wv >> 16), dot);
+    const float x0 = x_f16 ? half_bits_to_float(xv & 0xffffu) : bf16_bits_to_float(xv & 0xffffu);
+    const float x1 = x_f16 ? half_bits_to_float(xv >> 16) : bf16_bits_to_float(xv >> 16);
+    dot = fmaf(x0, bf16_bits_to_float(wv & 0xffffu), dot);
+    dot = fmaf(x1, bf16_bits_to_float(wv >> 16), dot);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(full, dot, o);

@@ -89,6 +89,11 @@ typedef struct es_moe_cfg {
                            *   2 = tensor-core path (tcgen05 grouped GEMM,
                            *       fp16 operands dequantised in shared
                            *       memory, fp16 per-pair rows)              */
+  int32_t x_dtype;        /* activations x: ES_DTYPE_BF16 (0, the model
+                           * dtype) or ES_DTYPE_F16 (the Expert Network's
+                           * wire dtype, protocol.py:3-9); fp16 x runs the
+                           * tensor-core path, which reads it without
+                           * rounding (kernel_path 1 rejects it)            */
 } es_moe_cfg;
 
 /* Per-projection MLX tensors for all experts of one layer, stacked on a
@@ -127,6 +132,21 @@ ES_API es_status es_moe_packed_bytes(const es_moe_cfg* cfg, size_t* bytes_out);
  * (src/mlx_expert_sniper/expert_io.py:420-436, engine.py:22-30). */
 ES_API es_status es_moe_prepare(const es_moe_cfg* cfg, const es_mlx_layer* layer,
                          void* packed, size_t packed_bytes, es_stream_t stream);
+
+/* The same repack from a streaming-format layer image already in device
+ * memory: the reference's layer_XX.bin minus its 16 KB JSON header, i.e.
+ * E fixed-size expert blocks of `block_bytes` each (a multiple of 16384),
+ * holding the nine tensors of TENSOR_ORDER (gate, up, down x weight,
+ * scales, biases) at `inner_offsets[0..8]` from the start of a block, fp16
+ * scales and biases. The shared expert, which the streaming files do not
+ * carry, comes from `shared_layer` (its shared_*_proj members) or NULL.
+ * Counterpart of the reader's pread + parse of one expert block
+ * (src/mlx_expert_sniper/expert_io.py:280-284, 338-362) and the writer's
+ * layout (src/mlx_expert_sniper/download.py:73-77, 197-212). */
+ES_API es_status es_moe_prepare_blocks(const es_moe_cfg* cfg, const void* blocks,
+                                       size_t block_bytes, const int64_t* inner_offsets,
+                                       const es_mlx_layer* shared_layer, void* packed,
+                                       size_t packed_bytes, es_stream_t stream);
 
 /* Workspace bytes needed by es_moe_forward / es_moe_expert_ffn for up to
  * `max_tokens` tokens per call (non-decreasing in max_tokens). The workspace

@@ -167,3 +167,24 @@ def test_tensor_path_full_shapes(cuda, name, T, bias):
     dec = MoEBlock(cfg.with_(kernel_path="decode"), packed=blk.packed, shared_gate_w=sg,
                    max_tokens=T).forward(x, logits, cb, out_dtype=torch.float32)
     assert_close_rms(out.cpu().numpy(), dec.cpu().numpy(), rel=TENSOR_REL, what="vs decode")
+
+
+def test_fp16_activations(cuda):
+    """x given in fp16 (es_moe_cfg.x_dtype, the Expert Network wire dtype):
+    read without rounding, against the oracle on the same fp16 values."""
+    cfg = SMALL.with_(x_dtype="f16")
+    lay, lay_np = _layer(cfg, 31, cuda)
+    T = 40
+    x, _, logits, sg = synthetic_inputs(cfg, T, seed=77, device=cuda)
+    x16 = (x.float() * 3.0).half()
+    blk = MoEBlock(cfg, weights=lay, shared_gate_w=sg, max_tokens=T)
+    out, idx, w = blk.forward(x16, logits, None, out_dtype=torch.float32, return_routing=True)
+    torch.cuda.synchronize()
+    assert blk.read_device_error() == 0
+    idx_n = idx.cpu().numpy()
+    w_ref = oracle_weights_for(idx_n, logits.float().cpu().numpy(), None, cfg.norm_topk_prob)
+    ref = co.expert_ffn(x16.float().cpu().numpy(), lay_np, idx_n, w_ref, sg.float().cpu().numpy())
+    err, rms = assert_close_rms(out.cpu().numpy(), ref, what="fp16 x")
+    assert err / rms < TENSOR_REL
+    with pytest.raises(ValueError):
+        blk.forward(x, logits)  # bf16 given to an fp16-x block
