@@ -1,0 +1,232 @@
+"""A Qwen3-MoE-shaped decoder around the MoE block: the caller side of the
+hot path.
+
+Restates the per-layer loop of the reference's `make_forward`
+(src/mlx_expert_sniper/generate.py:98-194) for batched decode on one GPU:
+
+  h = embed(tokens)
+  for each layer:
+      h = h + attention(rms_norm(h))                      (generate.py:112-118)
+      n = rms_norm(h)                                      (:120)
+      h = h + MoE block(n, gate(n) [+ cache bias])         (:121-178)
+  logits = lm_head(rms_norm(h))                            (:192-193)
+
+Attention is the Qwen3 one: q/k/v projections, RMS norm per head on q and
+k, rotary embedding (theta 1e6), grouped-query attention over a KV cache,
+output projection -- torch bf16 (scaled_dot_product_attention). The MoE
+block is MoEBlock (router, dispatch, 4-bit experts, combine; the kernels of
+this package). A whole decode step, all layers, is one CUDA graph: the
+position lives on the device (KV write index, rotary angle and attention
+mask are computed from it), so the same graph replays step after step.
+
+Weights are random (seeded): attention and embeddings bf16 N(0, 0.02),
+experts quantised MLX-affine 4-bit, norms 1; the KV cache holds a seeded
+N(0, 1) bf16 context. The model is a shape and timing stand-in, not a
+trained network.
+"""
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from .block import MoEBlock, prepare_packed
+from .config import MoEConfig, PRESETS
+from .quant import synthetic_layer
+
+
+@dataclass
+class DecoderConfig:
+    layers: int = 48
+    hidden: int = 2048
+    heads: int = 32
+    kv_heads: int = 4
+    head_dim: int = 128
+    vocab: int = 151936
+    rope_theta: float = 1e6
+    eps: float = 1e-6
+    moe: MoEConfig = field(default_factory=lambda: PRESETS["qwen3-30b-a3b"])
+    name: str = "qwen3-30b-a3b-decoder"
+
+
+QWEN3_30B_DECODER = DecoderConfig()
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
+
+
+def rope_tables(head_dim: int, max_pos: int, theta: float, device):
+    inv = theta ** (-torch.arange(0, head_dim, 2, device=device, dtype=torch.float64) / head_dim)
+    ang = torch.arange(max_pos, device=device, dtype=torch.float64)[:, None] * inv[None]
+    return ang.cos().float(), ang.sin().float()
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """x [..., head_dim]; rotate the two halves (the non-interleaved form)."""
+    h = x.shape[-1] // 2
+    x1, x2 = x[..., :h].float(), x[..., h:].float()
+    return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], -1).to(x.dtype)
+
+
+class Decoder:
+    """Batched decode: `batch` sequences, each with a `context`-token KV cache,
+    one new token per sequence per step."""
+
+    def __init__(self, dcfg: DecoderConfig, batch: int, context: int, max_steps: int = 64,
+                 seed: int = 0, device="cuda", expert_seed: int = 1000):
+        self.dcfg = dcfg
+        self.device = torch.device(device)
+        self.batch = batch
+        self.max_ctx = context + max_steps
+        D, H, KV, hd, V = dcfg.hidden, dcfg.heads, dcfg.kv_heads, dcfg.head_dim, dcfg.vocab
+        g = torch.Generator(device=self.device).manual_seed(seed)
+
+        def rnd(*shape, std=0.02):
+            return (torch.randn(shape, generator=g, device=self.device) * std).to(torch.bfloat16)
+
+        self.embed = rnd(V, D)
+        self.lm_head = rnd(V, D)
+        self.final_norm = torch.ones(D, dtype=torch.bfloat16, device=self.device)
+        self.layers = []
+        mcfg = dcfg.moe
+        self.ws = MoEBlock.new_workspace(mcfg, batch, self.device)
+        for l in range(dcfg.layers):
+            lay = synthetic_layer(mcfg, seed=expert_seed + l, device=self.device)
+            sg = rnd(D) if mcfg.has_shared else None
+            blk = MoEBlock(mcfg, packed=prepare_packed(mcfg, lay), shared_gate_w=sg,
+                           max_tokens=batch, workspace=self.ws)
+            del lay
+            self.layers.append({
+                "in_norm": torch.ones(D, dtype=torch.bfloat16, device=self.device),
+                "post_norm": torch.ones(D, dtype=torch.bfloat16, device=self.device),
+                "q": rnd(H * hd, D), "k": rnd(KV * hd, D), "v": rnd(KV * hd, D),
+                "o": rnd(D, H * hd),
+                "q_norm": torch.ones(hd, dtype=torch.bfloat16, device=self.device),
+                "k_norm": torch.ones(hd, dtype=torch.bfloat16, device=self.device),
+                "router": rnd(mcfg.num_experts, D),
+                "moe": blk,
+                "k_cache": torch.zeros(batch, KV, self.max_ctx, hd, dtype=torch.bfloat16,
+                                       device=self.device),
+                "v_cache": torch.zeros(batch, KV, self.max_ctx, hd, dtype=torch.bfloat16,
+                                       device=self.device),
+            })
+        # seeded N(0, 1) context in the caches
+        for L in self.layers:
+            L["k_cache"][:, :, :context] = torch.randn(
+                (batch, KV, context, hd), generator=g, device=self.device).to(torch.bfloat16)
+            L["v_cache"][:, :, :context] = torch.randn(
+                (batch, KV, context, hd), generator=g, device=self.device).to(torch.bfloat16)
+        self.cos, self.sin = rope_tables(hd, self.max_ctx, dcfg.rope_theta, self.device)
+        self.pos = torch.full((1,), context, dtype=torch.long, device=self.device)
+        self.ar = torch.arange(self.max_ctx, device=self.device)
+        self.tokens = torch.zeros(batch, dtype=torch.long, device=self.device)
+        self.logits = torch.empty(batch, V, dtype=torch.bfloat16, device=self.device)
+        self.cache_bias = [None] * dcfg.layers   # per-layer [E] routing bias, optional
+        self.graph = None
+
+    # -- one step, eager ----------------------------------------------------
+    def _attention(self, L: dict, x: torch.Tensor, cos, sin, mask) -> torch.Tensor:
+        c = self.dcfg
+        B, H, KV, hd = self.batch, c.heads, c.kv_heads, c.head_dim
+        q = (x @ L["q"].t()).view(B, H, hd)
+        k = (x @ L["k"].t()).view(B, KV, hd)
+        v = (x @ L["v"].t()).view(B, KV, hd)
+        q = apply_rope(rms_norm(q, L["q_norm"], c.eps), cos, sin)
+        k = apply_rope(rms_norm(k, L["k_norm"], c.eps), cos, sin)
+        L["k_cache"].index_copy_(2, self.pos, k.unsqueeze(2))
+        L["v_cache"].index_copy_(2, self.pos, v.unsqueeze(2))
+        o = F.scaled_dot_product_attention(q.unsqueeze(2), L["k_cache"], L["v_cache"],
+                                           attn_mask=mask, scale=1.0 / math.sqrt(hd),
+                                           enable_gqa=True)
+        return o.reshape(B, H * hd) @ L["o"].t()
+
+    def _step(self):
+        c = self.dcfg
+        h = self.embed.index_select(0, self.tokens)
+        cos = self.cos.index_select(0, self.pos)   # [1, hd/2]
+        sin = self.sin.index_select(0, self.pos)
+        # positions <= pos are visible
+        mask = torch.where(self.ar <= self.pos, 0.0, float("-inf")).to(torch.bfloat16)
+        mask = mask.view(1, 1, 1, -1)
+        for i, L in enumerate(self.layers):
+            h = h + self._attention(L, rms_norm(h, L["in_norm"], c.eps), cos, sin, mask)
+            n = rms_norm(h, L["post_norm"], c.eps)
+            logits = n @ L["router"].t()
+            h = h + L["moe"].forward(n, logits, self.cache_bias[i])
+        self.logits.copy_(rms_norm(h, self.final_norm, c.eps) @ self.lm_head.t())
+        self.pos.add_(1)
+
+    # -- graph ----------------------------------------------------------------
+    def capture(self):
+        """Capture one decode step (all layers) as a CUDA graph; the position
+        advances on the device at the end of every replay."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        p0 = self.pos.clone()
+        with torch.cuda.stream(s):
+            self._step()   # warm up (cuBLAS / SDPA workspaces) outside capture
+            torch.cuda.synchronize()
+            self.pos.copy_(p0)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=s):
+                self._step()
+        torch.cuda.synchronize()
+        self.pos.copy_(p0)
+        self._stream = s
+        return self
+
+    def step(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Feed one token per sequence; returns the next-token logits [B, V]."""
+        self.tokens.copy_(tokens)
+        if self.graph is None:
+            self._step()
+        else:
+            with torch.cuda.stream(self._stream):
+                self.graph.replay()
+            torch.cuda.current_stream(self.device).wait_stream(self._stream)
+        return self.logits
+
+
+def _bench(argv=None):
+    """Decode tokens/s of the 48-layer Qwen3-30B-shaped decoder (graph
+    replays, CUDA events) at batch 1 and 16 with a 2048-token context."""
+    import argparse
+    import json
+    ap = argparse.ArgumentParser(description="decoder decode throughput")
+    ap.add_argument("--batches", default="1,16")
+    ap.add_argument("--context", type=int, default=2048)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--layers", type=int, default=48)
+    args = ap.parse_args(argv)
+    res = {}
+    dcfg = DecoderConfig(layers=args.layers)
+    for B in [int(b) for b in args.batches.split(",")]:
+        t0 = time.time()
+        dec = Decoder(dcfg, B, args.context, max_steps=args.steps + 8).capture()
+        build_s = time.time() - t0
+        g = torch.Generator(device="cuda").manual_seed(B)
+        toks = torch.randint(0, dcfg.vocab, (B,), generator=g, device="cuda")
+        for _ in range(3):
+            toks = dec.step(toks).argmax(-1)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            toks = dec.step(toks).argmax(-1)
+        e1.record()
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        res[B] = {"ms_per_step": ms, "tokens_per_s": B / (ms * 1e-3), "build_s": build_s}
+        del dec
+        torch.cuda.empty_cache()
+    print(json.dumps({"decoder": dcfg.name, "layers": args.layers, "context": args.context,
+                      "results": res}))
+
+
+if __name__ == "__main__":
+    _bench()
