@@ -153,13 +153,16 @@ ES_DEV uint64_t l2_evict_first_policy() {
   return p;
 }
 
+// The waiting thread is suspended (issuing nothing) until the phase completes
+// or about a millisecond passes, so waiting warps leave the issue slots to
+// the warps that work.
 ES_DEV bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(phase)
+      : "r"(smem_addr(bar)), "r"(phase), "r"(1000000u)
       : "memory");
   return ok != 0;
 }
