@@ -54,7 +54,12 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--placement", default="hrw", choices=["hrw", "bounded"])
+    ap.add_argument("--placement", default="bounded", choices=["hrw", "bounded"],
+                    help="--gpus N > 1: expert placement over gpu0..gpuN-1: the reference's "
+                         "rendezvous hashing (hrw) or its capacity-bounded variant (bounded)")
+    ap.add_argument("--ep-graphs", action="store_true",
+                    help="--gpus N > 1: replay each layer's step (kernels + NCCL collectives) "
+                         "as a CUDA graph instead of launching eagerly")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
                     help="decode: the headline line (it also carries a short prefill "
                          "measurement); prefill: only the Qwen3-Next layer prefill")
@@ -559,8 +564,45 @@ def run_ours_ep(args):
 
     W = max(3, args.warmup)
     K = args.steps
-    for s in range(W):
-        step(s)
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        for s in range(max(W, L)):   # warm every layer (and NCCL) before capture
+            step(s)
+    torch.cuda.synchronize()
+    dist.barrier()
+    # one CUDA graph per layer holding the whole exchange (kernels and NCCL
+    # collectives); every rank must end up on the same path
+    graphs, note = [], "each layer's step (kernels + NCCL collectives) is a CUDA graph"
+    if args.ep_graphs:
+        try:
+            with torch.cuda.stream(stream):
+                for l in range(L):
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=stream):
+                        step(l)
+                    graphs.append(g)
+            ok = torch.ones(1, device=dev)
+        except Exception as exc:  # reported in the line, never silent
+            graphs, ok = [], torch.zeros(1, device=dev)
+            note = f"graph capture failed ({type(exc).__name__}); eager launches"
+        torch.cuda.synchronize()
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if float(ok.item()) < 1:
+            graphs = []
+            note = note if "failed" in note else "graph capture failed on a peer; eager launches"
+    else:
+        note = "eager launches (NCCL collectives not graph-captured; --ep-graphs captures them)"
+
+    def timed(s):
+        if graphs:
+            graphs[s % L].replay()
+        else:
+            step(s)
+
+    with torch.cuda.stream(stream):
+        for s in range(W):
+            timed(s)
     torch.cuda.synchronize()
     dist.barrier()
     clocks = ClockSampler(local_rank).start() if rank == 0 else None
@@ -568,10 +610,11 @@ def run_ours_ep(args):
     e1 = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     dist.barrier()
-    e0.record()
-    for s in range(W, W + K):
-        step(s)
-    e1.record()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for s in range(W, W + K):
+            timed(s)
+        e1.record(stream)
     e1.synchronize()
     ms = torch.tensor([e0.elapsed_time(e1) / K], device=dev)
     clk = clocks.stop() if clocks else None
@@ -622,9 +665,11 @@ def run_ours_ep(args):
             "gpu_launches": 7 * K,
             "clocks": clk,
             "cpu_baseline": None,
-            "note": "eager launches (NCCL calls are not graph-captured)",
+            "note": note,
         }
         print(json.dumps(line), flush=True)
+    del graphs  # graphs holding NCCL calls go before the process group
+    torch.cuda.synchronize()
     del backends
     dist.barrier()
     dist.destroy_process_group()
