@@ -66,6 +66,8 @@ def parse_args():
     ap.add_argument("--prefill-tokens", type=int, default=4096)
     ap.add_argument("--prefill-steps", type=int, default=50)
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-decoder", action="store_true",
+                    help="skip the 48-layer decoder measurement in the decode line")
     return ap.parse_args()
 
 
@@ -511,6 +513,14 @@ def run_ours_single(args):
     if not args.no_prefill:
         line["prefill"] = measure_prefill(args.prefill_tokens, min(args.prefill_steps, 50),
                                           3)
+    if not args.no_decoder:
+        # the Qwen3-30B-shaped 48-layer decoder around the block (attention,
+        # norms, rotary, KV cache with a 2048-token context; one CUDA graph
+        # per step): whole-model decode tokens/s at batch 1 and 16
+        from expert_sniper_b200.decoder import measure as measure_decoder
+        del blocks, packed
+        torch.cuda.empty_cache()
+        line["decoder"] = measure_decoder((1, 16), 2048, 40, 48)
     print(json.dumps(line), flush=True)
 
 

@@ -192,6 +192,34 @@ class Decoder:
         return self.logits
 
 
+def measure(batches=(1, 16), context: int = 2048, steps: int = 40, layers: int = 48) -> dict:
+    """Decode tokens/s of the Qwen3-30B-shaped decoder: graph replays with
+    greedy next tokens, timed with CUDA events after 3 warm-up steps."""
+    dcfg = DecoderConfig(layers=layers)
+    res = {}
+    for B in batches:
+        t0 = time.time()
+        dec = Decoder(dcfg, B, context, max_steps=steps + 8).capture()
+        build_s = time.time() - t0
+        g = torch.Generator(device="cuda").manual_seed(B)
+        toks = torch.randint(0, dcfg.vocab, (B,), generator=g, device="cuda")
+        for _ in range(3):
+            toks = dec.step(toks).argmax(-1)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            toks = dec.step(toks).argmax(-1)
+        e1.record()
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        res[str(B)] = {"ms_per_step": ms, "tokens_per_s": B / (ms * 1e-3), "build_s": build_s}
+        del dec
+        torch.cuda.empty_cache()
+    return {"decoder": dcfg.name, "layers": layers, "context": context, "steps": steps,
+            "results": res}
+
+
 def _bench(argv=None):
     """Decode tokens/s of the 48-layer Qwen3-30B-shaped decoder (graph
     replays, CUDA events) at batch 1 and 16 with a 2048-token context."""
@@ -203,29 +231,8 @@ def _bench(argv=None):
     ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--layers", type=int, default=48)
     args = ap.parse_args(argv)
-    res = {}
-    dcfg = DecoderConfig(layers=args.layers)
-    for B in [int(b) for b in args.batches.split(",")]:
-        t0 = time.time()
-        dec = Decoder(dcfg, B, args.context, max_steps=args.steps + 8).capture()
-        build_s = time.time() - t0
-        g = torch.Generator(device="cuda").manual_seed(B)
-        toks = torch.randint(0, dcfg.vocab, (B,), generator=g, device="cuda")
-        for _ in range(3):
-            toks = dec.step(toks).argmax(-1)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            toks = dec.step(toks).argmax(-1)
-        e1.record()
-        e1.synchronize()
-        ms = e0.elapsed_time(e1) / args.steps
-        res[B] = {"ms_per_step": ms, "tokens_per_s": B / (ms * 1e-3), "build_s": build_s}
-        del dec
-        torch.cuda.empty_cache()
-    print(json.dumps({"decoder": dcfg.name, "layers": args.layers, "context": args.context,
-                      "results": res}))
+    print(json.dumps(measure([int(b) for b in args.batches.split(",")], args.context,
+                             args.steps, args.layers)))
 
 
 if __name__ == "__main__":
