@@ -136,3 +136,31 @@ def test_http_compute_bin_round_trip():
     finally:
         server.should_exit = True
         th.join(timeout=10)
+
+
+def test_four_nodes_sum_to_the_block():
+    """Every node answers for its HRW partition; the driver sums the fp16
+    partials in fixed node order in fp32 (reader.py:278-292): the total is the
+    whole block up to the fp16 rounding of each partial."""
+    from expert_sniper_b200 import hrw
+    lay = {k: v.numpy() for k, v in synthetic_layer(CFG, seed=8).items()}
+    roster = hrw.gpu_roster(4)
+    plan = hrw.plan(roster, CFG.num_experts)
+    rng = np.random.default_rng(9)
+    T = 7
+    h = rng.standard_normal((1, T, CFG.hidden)).astype(np.float16)
+    inds = np.stack([rng.choice(CFG.num_experts, CFG.top_k, replace=False)
+                     for _ in range(T)])[None].astype(np.int32)
+    w = rng.random((1, T, CFG.top_k)).astype(np.float32)
+    ids = sorted(set(inds.ravel().tolist()))
+    total = np.zeros((T, CFG.hidden), np.float32)
+    counted = 0
+    for name in roster:
+        node = _OracleNode(lay, sorted(plan[name]))
+        n, part = nd.unpack_response(node.handle(nd.pack_request(0, ids, h, inds, w)))
+        counted += n
+        total += part[0].astype(np.float32)
+    assert counted == len(ids)
+    full = mo.expert_ffn(h[0].astype(np.float32), {k: v for k, v in lay.items()
+                                                   if k.startswith("switch_mlp")}, inds[0], w[0])
+    assert_close_rms(total, full, rel=1e-2, what="sum of 4 nodes")
