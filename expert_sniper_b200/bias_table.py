@@ -31,13 +31,19 @@ class CacheBiasTable:
         self._stream = torch.cuda.Stream(self.device) if on_gpu else None
         self._ready = None
 
-    def row(self, layer: int):
-        """The [E] device bias of one layer, or None when bias <= 0."""
-        if self.bias <= 0:
-            return None
+    def sync(self) -> None:
+        """Order the current stream after pending row updates (call before
+        replaying a graph that reads the table)."""
         if self._ready is not None:
             torch.cuda.current_stream(self.device).wait_event(self._ready)
             self._ready = None
+
+    def row(self, layer: int):
+        """The [E] device bias of one layer, or None when bias <= 0. Its
+        address is fixed, so a captured graph keeps reading the live row."""
+        if self.bias <= 0:
+            return None
+        self.sync()
         return self.table[layer]
 
     def set_cached(self, layer: int, cached_ids) -> None:

@@ -397,7 +397,8 @@ es_status es_moe_read_error(const void* workspace, int32_t clear, uint32_t* flag
   uint32_t v = 0;
   if (cudaMemcpyAsync(&v, workspace, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) return ES_ERR_CUDA;
   if (cudaStreamSynchronize(st) != cudaSuccess) return ES_ERR_CUDA;
-  if (clear && cudaMemsetAsync(const_cast<void*>(workspace), 0, 4, st) != cudaSuccess)
+  // clearing also drops the recorded site of a timed-out wait (words 1-3)
+  if (clear && cudaMemsetAsync(const_cast<void*>(workspace), 0, 16, st) != cudaSuccess)
     return ES_ERR_CUDA;
   *flags_out = v;
   return ES_OK;

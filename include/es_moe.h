@@ -264,7 +264,10 @@ ES_API es_status es_moe_forward_noalloc(const es_moe_cfg* cfg, const void* x,
                                         es_stream_t stream);
 
 /* Synchronously read (and clear when `clear` != 0) the device error word of
- * a workspace. Blocks the host on `stream`. */
+ * a workspace. Blocks the host on `stream`. When ES_DEVERR_TIMEOUT is set by
+ * the tensor-core kernels, the next three 32-bit words of the workspace hold
+ * the first timed-out wait since they were last cleared (site id, CTA, stage
+ * or unit); clearing resets them too. No reference counterpart. */
 ES_API es_status es_moe_read_error(const void* workspace, int32_t clear,
                             uint32_t* flags_out, es_stream_t stream);
 

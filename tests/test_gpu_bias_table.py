@@ -40,7 +40,7 @@ def test_graph_reads_updated_row(cuda):
     routed = []
     for cached in ([0, 1, 2, 3], [28, 29, 30, 31]):
         table.set_cached(1, cached)
-        torch.cuda.current_stream().wait_event(table._ready) if table._ready else None
+        table.sync()
         with torch.cuda.stream(s):
             s.wait_stream(torch.cuda.current_stream())
             g.replay()
