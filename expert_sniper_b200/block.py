@@ -221,9 +221,17 @@ class MoEBlock:
         return out
 
     def expert_ffn(self, x: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor,
-                   out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor = None):
-        """Experts + combine for given routing (-1 ids are skipped)."""
+                   out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor = None,
+                   kernel_path: str = None):
+        """Experts + combine for given routing (-1 ids are skipped).
+        `kernel_path` ("auto", "decode", "tensor") overrides the block's
+        config for this call (e.g. when most slots are masked, the caller
+        knows the real number of pairs per expert better than the row count
+        does)."""
         cfg = self.cfg
+        ccfg = self.ccfg
+        if kernel_path is not None and kernel_path != cfg.kernel_path:
+            ccfg = cfg.with_(kernel_path=kernel_path).to_c()
         xf = self._flat(x, cfg.hidden, "x")
         want = torch.float16 if cfg.x_dtype == "f16" else torch.bfloat16
         if xf.dtype != want:
@@ -235,7 +243,7 @@ class MoEBlock:
         if out is None:
             out = torch.empty((T, cfg.hidden), dtype=out_dtype, device=self.device)
         _native.check("es_moe_expert_ffn", _native.lib().es_moe_expert_ffn(
-            ctypes.byref(self.ccfg), xf.data_ptr(), idx.data_ptr(), w.data_ptr(),
+            ctypes.byref(ccfg), xf.data_ptr(), idx.data_ptr(), w.data_ptr(),
             _ptr(self.shared_gate_w), self.packed.data_ptr(), out.data_ptr(), _DT_CODE[out.dtype],
             T, self._ws.data_ptr(), self._ws.numel(), _stream(self.device)))
         return out.reshape(*x.shape[:-1], cfg.hidden)
