@@ -173,7 +173,6 @@ KERNELS = ["front", "gap", "gateup", "down", "combine"]
 # --------------------------------------------------------------------------- #
 
 def cpu_baseline(cfg, T, seconds, layer_np=None, seed=0):
-    import numpy as np
     from expert_sniper_b200.quant import cache_bias_vector, synthetic_inputs, synthetic_layer
     from oracle import c_oracle
     c_oracle.build()

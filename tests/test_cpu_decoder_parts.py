@@ -3,8 +3,6 @@ and the half-split rotation against their defining formulas (the decoder
 itself runs on the GPU; tests/test_gpu_decoder.py compares whole steps)."""
 from __future__ import annotations
 
-import math
-
 import numpy as np
 import torch
 

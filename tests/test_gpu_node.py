@@ -11,7 +11,6 @@ import urllib.request
 
 import numpy as np
 import pytest
-import torch
 
 from expert_sniper_b200 import hrw
 from expert_sniper_b200 import node as nd
