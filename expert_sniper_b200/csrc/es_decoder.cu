@@ -1,0 +1,136 @@
+// Caller-side helpers for the decoder around the MoE block (the per-layer
+// loop of src/mlx_expert_sniper/generate.py:114-122): fused residual add +
+// RMS norm, and the per-head q/k RMS norm + rotary embedding + KV-cache write
+// of Qwen3 attention. Plain elementwise/reduction kernels in fp32 arithmetic
+// on bf16 tensors; no counterpart in the reference beyond the MLX ops they
+// fuse.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "es_moe.h"
+
+namespace {
+
+__device__ __forceinline__ float bf(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
+__device__ __forceinline__ uint16_t to_bf(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+__device__ __forceinline__ float block_sum(float v, float* s_warp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (lane == 0) s_warp[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  const int nw = (blockDim.x + 31) >> 5;
+  for (int i = 0; i < nw; ++i) t += s_warp[i];
+  __syncthreads();
+  return t;
+}
+
+// one block per row: h += delta (if any); out = h * rsqrt(mean(h^2) + eps) * w
+__global__ void add_rmsnorm_kernel(uint16_t* h, const uint16_t* delta, const uint16_t* w,
+                                   uint16_t* out, int cols, float eps) {
+  __shared__ float s_warp[32];
+  const size_t base = (size_t)blockIdx.x * cols;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    float v = bf(h[base + c]);
+    if (delta) {
+      v += bf(delta[base + c]);
+      h[base + c] = to_bf(v);  // the residual stream stays bf16, as the model's
+      v = bf(h[base + c]);
+    }
+    ss += v * v;
+  }
+  const float r = rsqrtf(block_sum(ss, s_warp) / cols + eps);
+  for (int c = threadIdx.x; c < cols; c += blockDim.x)
+    out[base + c] = to_bf(bf(h[base + c]) * r * bf(w[c]));
+}
+
+// one warp per (token, head) of the fused projection output
+// qkv [B, (H + 2 KV) * hd]: RMS norm over hd (q and k heads), rotary on the
+// two halves, q -> q_out [B, H, hd]; k, v -> caches [B, KV, max_ctx, hd] at
+// position *pos
+__global__ void qk_norm_rope_kv_kernel(const uint16_t* qkv, const uint16_t* qn, const uint16_t* kn,
+                                       const float* cos_t, const float* sin_t, const int64_t* pos,
+                                       uint16_t* q_out, uint16_t* kc, uint16_t* vc, int B, int H,
+                                       int KV, int hd, int max_ctx, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int heads = H + 2 * KV;
+  if (item >= B * heads) return;
+  const int b = item / heads, hh = item - b * heads;
+  const long long pl = *pos;
+  if (pl < 0 || pl >= max_ctx) return;  // outside the cache: nothing written
+  const int p = (int)pl;
+  const uint16_t* src = qkv + (size_t)b * heads * hd + (size_t)hh * hd;
+  const int half = hd >> 1;
+  if (hh >= H + KV) {  // v head: copy into the cache
+    const int kvh = hh - H - KV;
+    uint16_t* dst = vc + (((size_t)b * KV + kvh) * max_ctx + p) * hd;
+    for (int i = lane; i < hd; i += 32) dst[i] = src[i];
+    return;
+  }
+  float ss = 0.f;
+  for (int i = lane; i < hd; i += 32) {
+    const float v = bf(src[i]);
+    ss += v * v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / hd + eps);
+  const uint16_t* nw = hh < H ? qn : kn;
+  uint16_t* dst = hh < H ? q_out + ((size_t)b * H + hh) * hd
+                         : kc + (((size_t)b * KV + (hh - H)) * max_ctx + p) * hd;
+  const float* cs = cos_t + (size_t)p * half;
+  const float* sn = sin_t + (size_t)p * half;
+  for (int i = lane; i < half; i += 32) {
+    // round to bf16 after the norm, as the unfused path does
+    const float x1 = bf(to_bf(bf(src[i]) * r * bf(nw[i])));
+    const float x2 = bf(to_bf(bf(src[i + half]) * r * bf(nw[i + half])));
+    dst[i] = to_bf(x1 * cs[i] - x2 * sn[i]);
+    dst[i + half] = to_bf(x2 * cs[i] + x1 * sn[i]);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+es_status es_dec_add_rmsnorm(void* h, const void* delta, const void* weight, void* out,
+                             int32_t rows, int32_t cols, float eps, es_stream_t stream) {
+  if (!h || !weight || !out || rows < 0 || cols <= 0) return ES_ERR_INVALID_ARG;
+  if (rows == 0) return ES_OK;
+  const int threads = cols >= 1024 ? 256 : 128;
+  add_rmsnorm_kernel<<<rows, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint16_t*>(h), static_cast<const uint16_t*>(delta),
+      static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), cols, eps);
+  return cudaGetLastError() == cudaSuccess ? ES_OK : ES_ERR_CUDA;
+}
+
+es_status es_dec_qk_norm_rope_kv(const void* qkv, const void* q_norm, const void* k_norm,
+                                 const float* cos_table, const float* sin_table,
+                                 const int64_t* pos, void* q_out, void* k_cache, void* v_cache,
+                                 int32_t batch, int32_t heads, int32_t kv_heads,
+                                 int32_t head_dim, int32_t max_ctx, float eps,
+                                 es_stream_t stream) {
+  if (!qkv || !q_norm || !k_norm || !cos_table || !sin_table || !pos || !q_out || !k_cache ||
+      !v_cache || batch < 0 || heads <= 0 || kv_heads <= 0 || head_dim <= 0 || head_dim % 2 ||
+      max_ctx <= 0)
+    return ES_ERR_INVALID_ARG;
+  if (batch == 0) return ES_OK;
+  const int items = batch * (heads + 2 * kv_heads);
+  const int warps = 8;
+  qk_norm_rope_kv_kernel<<<(items + warps - 1) / warps, warps * 32, 0,
+                           static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(qkv), static_cast<const uint16_t*>(q_norm),
+      static_cast<const uint16_t*>(k_norm), cos_table, sin_table, pos,
+      static_cast<uint16_t*>(q_out), static_cast<uint16_t*>(k_cache),
+      static_cast<uint16_t*>(v_cache), batch, heads, kv_heads, head_dim, max_ctx, eps);
+  return cudaGetLastError() == cudaSuccess ? ES_OK : ES_ERR_CUDA;
+}
+
+}  // extern "C"

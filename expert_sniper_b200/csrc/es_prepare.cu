@@ -22,21 +22,21 @@ __global__ void __launch_bounds__(kWarps * 32) prepare_kernel(PrepareArgs a, lon
   const long long per_expert = gu_tiles + (long long)(D / 16) * GI;
   const int e = (int)(wg / per_expert);
   const long long t = wg - (long long)e * per_expert;
-  int proj, rb, G, N, K;
+  int proj, rb, G, K;
   size_t dst_off;
   if (t < gu_tiles) {
     rb = (int)(t / (GD * 2));
     const int rem = (int)(t - (long long)rb * GD * 2);
     G = rem >> 1;
     proj = rem & 1;
-    N = I; K = D;
+    K = D;
     dst_off = gateup_tile_off(GD, rb, G, proj);
   } else {
     const long long t2 = t - gu_tiles;
     rb = (int)(t2 / GI);
     G = (int)(t2 - (long long)rb * GI);
     proj = 2;
-    N = D; K = I;
+    K = I;
     dst_off = down_tile_off(D, I, rb, G);
   }
   const bool shared = e >= a.E;

@@ -13,11 +13,20 @@ Restates the per-layer loop of the reference's `make_forward`
 
 Attention is the Qwen3 one: q/k/v projections, RMS norm per head on q and
 k, rotary embedding (theta 1e6), grouped-query attention over a KV cache,
-output projection -- torch bf16 (scaled_dot_product_attention). The MoE
-block is MoEBlock (router, dispatch, 4-bit experts, combine; the kernels of
-this package). A whole decode step, all layers, is one CUDA graph: the
-position lives on the device (KV write index, rotary angle and attention
-mask are computed from it), so the same graph replays step after step.
+output projection. The MoE block is MoEBlock (router, dispatch, 4-bit
+experts, combine; the kernels of this package). A whole decode step, all
+layers, is one CUDA graph: the position lives on the device (KV write index,
+rotary angle and attention mask are computed from it), so the same graph
+replays step after step.
+
+Two forms of the code around the block, same arithmetic (fp32 math on bf16
+tensors, bf16 rounding at the same points):
+  fused=True   one q|k|v projection GEMM; the residual add + RMS norm and
+               the q/k norm + rotary + cache write are single kernels of
+               libes_moe.so (es_dec_add_rmsnorm, es_dec_qk_norm_rope_kv);
+  fused=False  the same steps as separate torch ops (the restatement the
+               fused kernels are checked against).
+Attention itself is torch's scaled_dot_product_attention in both.
 
 Weights are random (seeded): attention and embeddings bf16 N(0, 0.02),
 experts quantised MLX-affine 4-bit, norms 1; the KV cache holds a seeded
@@ -30,9 +39,12 @@ import math
 import time
 from dataclasses import dataclass, field
 
+import ctypes
+
 import torch
 import torch.nn.functional as F
 
+from . import _native
 from .block import MoEBlock, prepare_packed
 from .config import MoEConfig, PRESETS
 from .quant import synthetic_layer
@@ -73,13 +85,56 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], -1).to(x.dtype)
 
 
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def add_rmsnorm_(h: torch.Tensor, delta, w: torch.Tensor, out: torch.Tensor,
+                 eps: float) -> torch.Tensor:
+    """h += delta (bf16, in place; skipped when delta is None), then
+    out = rms_norm(h, w): one es_dec_add_rmsnorm launch."""
+    rows, cols = h.shape
+    for t in (h, w, out) + ((delta,) if delta is not None else ()):
+        if not (t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous()):
+            raise ValueError("add_rmsnorm_ takes contiguous bf16 CUDA tensors")
+    if out.shape != h.shape or w.numel() != cols or (delta is not None and delta.shape != h.shape):
+        raise ValueError("add_rmsnorm_: shape mismatch")
+    _native.check("es_dec_add_rmsnorm", _native.lib().es_dec_add_rmsnorm(
+        h.data_ptr(), 0 if delta is None else delta.data_ptr(), w.data_ptr(), out.data_ptr(),
+        rows, cols, ctypes.c_float(eps), _stream(h)))
+    return out
+
+
+def qk_norm_rope_kv(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor,
+                    cos: torch.Tensor, sin: torch.Tensor, pos: torch.Tensor, q_out: torch.Tensor,
+                    k_cache: torch.Tensor, v_cache: torch.Tensor, eps: float) -> torch.Tensor:
+    """qkv [B, (H + 2 KV) * hd] -> q_out [B, H, hd] (normed, rotated); the
+    normed, rotated k and the v of every sequence written into the caches
+    [B, KV, max_ctx, hd] at position pos (a device int64 scalar tensor)."""
+    B, H, hd = q_out.shape
+    KV, max_ctx = k_cache.shape[1], k_cache.shape[2]
+    if qkv.shape != (B, (H + 2 * KV) * hd) or v_cache.shape != k_cache.shape:
+        raise ValueError("qk_norm_rope_kv: shape mismatch")
+    if cos.shape != (max_ctx, hd // 2) or sin.shape != cos.shape or pos.dtype != torch.int64:
+        raise ValueError("qk_norm_rope_kv: rotary tables must be [max_ctx, hd/2] f32")
+    for t in (qkv, q_norm, k_norm, q_out, k_cache, v_cache, cos, sin, pos):
+        if not (t.is_cuda and t.is_contiguous()):
+            raise ValueError("qk_norm_rope_kv takes contiguous CUDA tensors")
+    _native.check("es_dec_qk_norm_rope_kv", _native.lib().es_dec_qk_norm_rope_kv(
+        qkv.data_ptr(), q_norm.data_ptr(), k_norm.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+        pos.data_ptr(), q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), B, H, KV, hd,
+        max_ctx, ctypes.c_float(eps), _stream(qkv)))
+    return q_out
+
+
 class Decoder:
     """Batched decode: `batch` sequences, each with a `context`-token KV cache,
     one new token per sequence per step."""
 
     def __init__(self, dcfg: DecoderConfig, batch: int, context: int, max_steps: int = 64,
-                 seed: int = 0, device="cuda", expert_seed: int = 1000):
+                 seed: int = 0, device="cuda", expert_seed: int = 1000, fused: bool = True):
         self.dcfg = dcfg
+        self.fused = fused
         self.device = torch.device(device)
         self.batch = batch
         self.max_ctx = context + max_steps
@@ -104,7 +159,8 @@ class Decoder:
             self.layers.append({
                 "in_norm": torch.ones(D, dtype=torch.bfloat16, device=self.device),
                 "post_norm": torch.ones(D, dtype=torch.bfloat16, device=self.device),
-                "q": rnd(H * hd, D), "k": rnd(KV * hd, D), "v": rnd(KV * hd, D),
+                # q, k and v projections stacked as one [(H + 2 KV) hd, D] matrix
+                "qkv": torch.cat([rnd(H * hd, D), rnd(KV * hd, D), rnd(KV * hd, D)]),
                 "o": rnd(D, H * hd),
                 "q_norm": torch.ones(hd, dtype=torch.bfloat16, device=self.device),
                 "k_norm": torch.ones(hd, dtype=torch.bfloat16, device=self.device),
@@ -126,39 +182,70 @@ class Decoder:
         self.ar = torch.arange(self.max_ctx, device=self.device)
         self.tokens = torch.zeros(batch, dtype=torch.long, device=self.device)
         self.logits = torch.empty(batch, V, dtype=torch.bfloat16, device=self.device)
+        self.h = torch.empty(batch, D, dtype=torch.bfloat16, device=self.device)
+        self.n = torch.empty(batch, D, dtype=torch.bfloat16, device=self.device)
+        self.q = torch.empty(batch, H, hd, dtype=torch.bfloat16, device=self.device)
         self.cache_bias = [None] * dcfg.layers   # per-layer [E] routing bias, optional
         self.graph = None
 
     # -- one step, eager ----------------------------------------------------
-    def _attention(self, L: dict, x: torch.Tensor, cos, sin, mask) -> torch.Tensor:
-        c = self.dcfg
-        B, H, KV, hd = self.batch, c.heads, c.kv_heads, c.head_dim
-        q = (x @ L["q"].t()).view(B, H, hd)
-        k = (x @ L["k"].t()).view(B, KV, hd)
-        v = (x @ L["v"].t()).view(B, KV, hd)
-        q = apply_rope(rms_norm(q, L["q_norm"], c.eps), cos, sin)
-        k = apply_rope(rms_norm(k, L["k_norm"], c.eps), cos, sin)
-        L["k_cache"].index_copy_(2, self.pos, k.unsqueeze(2))
-        L["v_cache"].index_copy_(2, self.pos, v.unsqueeze(2))
+    def _sdpa(self, L: dict, q: torch.Tensor, mask) -> torch.Tensor:
+        B, H, hd = q.shape
         o = F.scaled_dot_product_attention(q.unsqueeze(2), L["k_cache"], L["v_cache"],
                                            attn_mask=mask, scale=1.0 / math.sqrt(hd),
                                            enable_gqa=True)
         return o.reshape(B, H * hd) @ L["o"].t()
 
+    def _attention(self, L: dict, x: torch.Tensor, cos, sin, mask) -> torch.Tensor:
+        c = self.dcfg
+        B, H, KV, hd = self.batch, c.heads, c.kv_heads, c.head_dim
+        w = L["qkv"]
+        q = (x @ w[:H * hd].t()).view(B, H, hd)
+        k = (x @ w[H * hd:(H + KV) * hd].t()).view(B, KV, hd)
+        v = (x @ w[(H + KV) * hd:].t()).view(B, KV, hd)
+        q = apply_rope(rms_norm(q, L["q_norm"], c.eps), cos, sin)
+        k = apply_rope(rms_norm(k, L["k_norm"], c.eps), cos, sin)
+        L["k_cache"].index_copy_(2, self.pos, k.unsqueeze(2))
+        L["v_cache"].index_copy_(2, self.pos, v.unsqueeze(2))
+        return self._sdpa(L, q, mask)
+
+    def _mask(self):
+        # positions <= pos are visible
+        mask = torch.where(self.ar <= self.pos, 0.0, float("-inf")).to(torch.bfloat16)
+        return mask.view(1, 1, 1, -1)
+
     def _step(self):
+        if self.fused:
+            return self._step_fused()
         c = self.dcfg
         h = self.embed.index_select(0, self.tokens)
         cos = self.cos.index_select(0, self.pos)   # [1, hd/2]
         sin = self.sin.index_select(0, self.pos)
-        # positions <= pos are visible
-        mask = torch.where(self.ar <= self.pos, 0.0, float("-inf")).to(torch.bfloat16)
-        mask = mask.view(1, 1, 1, -1)
+        mask = self._mask()
         for i, L in enumerate(self.layers):
             h = h + self._attention(L, rms_norm(h, L["in_norm"], c.eps), cos, sin, mask)
             n = rms_norm(h, L["post_norm"], c.eps)
             logits = n @ L["router"].t()
             h = h + L["moe"].forward(n, logits, self.cache_bias[i])
         self.logits.copy_(rms_norm(h, self.final_norm, c.eps) @ self.lm_head.t())
+        self.pos.add_(1)
+
+    def _step_fused(self):
+        c = self.dcfg
+        h, n = self.h, self.n
+        torch.index_select(self.embed, 0, self.tokens, out=h)
+        mask = self._mask()
+        delta = None
+        for i, L in enumerate(self.layers):
+            add_rmsnorm_(h, delta, L["in_norm"], n, c.eps)
+            qkv_proj = n @ L["qkv"].t()
+            qk_norm_rope_kv(qkv_proj, L["q_norm"], L["k_norm"], self.cos, self.sin, self.pos,
+                            self.q, L["k_cache"], L["v_cache"], c.eps)
+            add_rmsnorm_(h, self._sdpa(L, self.q, mask), L["post_norm"], n, c.eps)
+            logits = n @ L["router"].t()
+            delta = L["moe"].forward(n, logits, self.cache_bias[i])
+        add_rmsnorm_(h, delta, self.final_norm, n, c.eps)
+        torch.matmul(n, self.lm_head.t(), out=self.logits)
         self.pos.add_(1)
 
     # -- graph ----------------------------------------------------------------
@@ -192,14 +279,15 @@ class Decoder:
         return self.logits
 
 
-def measure(batches=(1, 16), context: int = 2048, steps: int = 40, layers: int = 48) -> dict:
+def measure(batches=(1, 16), context: int = 2048, steps: int = 40, layers: int = 48,
+            fused: bool = True) -> dict:
     """Decode tokens/s of the Qwen3-30B-shaped decoder: graph replays with
     greedy next tokens, timed with CUDA events after 3 warm-up steps."""
     dcfg = DecoderConfig(layers=layers)
     res = {}
     for B in batches:
         t0 = time.time()
-        dec = Decoder(dcfg, B, context, max_steps=steps + 8).capture()
+        dec = Decoder(dcfg, B, context, max_steps=steps + 8, fused=fused).capture()
         build_s = time.time() - t0
         g = torch.Generator(device="cuda").manual_seed(B)
         toks = torch.randint(0, dcfg.vocab, (B,), generator=g, device="cuda")
@@ -217,7 +305,7 @@ def measure(batches=(1, 16), context: int = 2048, steps: int = 40, layers: int =
         del dec
         torch.cuda.empty_cache()
     return {"decoder": dcfg.name, "layers": layers, "context": context, "steps": steps,
-            "results": res}
+            "fused": fused, "results": res}
 
 
 def _bench(argv=None):
@@ -230,9 +318,11 @@ def _bench(argv=None):
     ap.add_argument("--context", type=int, default=2048)
     ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--unfused", action="store_true",
+                    help="torch ops around the block instead of the fused helper kernels")
     args = ap.parse_args(argv)
     print(json.dumps(measure([int(b) for b in args.batches.split(",")], args.context,
-                             args.steps, args.layers)))
+                             args.steps, args.layers, fused=not args.unfused)))
 
 
 if __name__ == "__main__":

@@ -271,6 +271,34 @@ ES_API es_status es_moe_forward_noalloc(const es_moe_cfg* cfg, const void* x,
 ES_API es_status es_moe_read_error(const void* workspace, int32_t clear,
                             uint32_t* flags_out, es_stream_t stream);
 
+/* ---- decoder helpers: the caller's per-layer loop around the block ------
+ * bf16 tensors, fp32 arithmetic. Counterparts of the MLX ops of the layer
+ * loop in src/mlx_expert_sniper/generate.py:114-122 (input_layernorm,
+ * residual adds, post_attention_layernorm) and of Qwen3 attention's q/k
+ * norm + rotary + cache update (mlx_lm qwen3_moe Attention, called at
+ * generate.py:118). */
+
+/* For each of `rows` rows of `cols`: if delta != NULL, h += delta (rounded
+ * to bf16 in place); then out = h * rsqrt(mean(h^2) + eps) * weight. */
+ES_API es_status es_dec_add_rmsnorm(void* h, const void* delta, const void* weight,
+                                    void* out, int32_t rows, int32_t cols, float eps,
+                                    es_stream_t stream);
+
+/* qkv [batch][(heads + 2*kv_heads) * head_dim] is one fused projection
+ * (q heads, then k heads, then v heads). q and k heads get an RMS norm over
+ * head_dim (weights q_norm / k_norm, result rounded to bf16) and the rotary
+ * embedding of position *pos (device int64) on their two halves, from
+ * cos_table / sin_table [max_ctx][head_dim/2] f32. q goes to q_out
+ * [batch][heads][head_dim]; k and v are written to k_cache / v_cache
+ * [batch][kv_heads][max_ctx][head_dim] at *pos. Requires *pos < max_ctx. */
+ES_API es_status es_dec_qk_norm_rope_kv(const void* qkv, const void* q_norm,
+                                        const void* k_norm, const float* cos_table,
+                                        const float* sin_table, const int64_t* pos,
+                                        void* q_out, void* k_cache, void* v_cache,
+                                        int32_t batch, int32_t heads, int32_t kv_heads,
+                                        int32_t head_dim, int32_t max_ctx, float eps,
+                                        es_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -92,6 +92,16 @@ def test_null_and_size_checks_return_status(lib):
                                  None) == 1
     # read_error validates before touching the device
     assert lib.es_moe_read_error(None, 0, None, None) == 1
+    # decoder helpers: null pointers and bad shapes are rejected before a
+    # launch; zero rows / batch is a no-op success
+    assert lib.es_dec_add_rmsnorm(None, None, None, None, 4, 256, 1e-6, None) == 1
+    assert lib.es_dec_add_rmsnorm(16, None, 16, 16, 4, 0, 1e-6, None) == 1
+    assert lib.es_dec_add_rmsnorm(16, None, 16, 16, 0, 256, 1e-6, None) == 0
+    args = [16] * 9
+    assert lib.es_dec_qk_norm_rope_kv(*args, 2, 4, 2, 63, 8, 1e-6, None) == 1  # odd head_dim
+    assert lib.es_dec_qk_norm_rope_kv(*args, 2, 4, 2, 64, 0, 1e-6, None) == 1
+    assert lib.es_dec_qk_norm_rope_kv(*([None] + args[1:]), 2, 4, 2, 64, 8, 1e-6, None) == 1
+    assert lib.es_dec_qk_norm_rope_kv(*args, 0, 4, 2, 64, 8, 1e-6, None) == 0
 
 
 def test_config_validation_in_python():

@@ -42,9 +42,10 @@ def _ref_step(dec: Decoder, caches, tokens, pos, expert_seed=1000):
     h = f(dec.embed[tokens])
     for l, L in enumerate(dec.layers):
         x = norm(h, L["in_norm"])
-        q = rope(norm((x @ f(L["q"]).t()).view(B, H, hd), L["q_norm"]))
-        k = rope(norm((x @ f(L["k"]).t()).view(B, KV, hd), L["k_norm"]))
-        v = (x @ f(L["v"]).t()).view(B, KV, hd)
+        wq, wk, wv = f(L["qkv"]).split([H * hd, KV * hd, KV * hd])
+        q = rope(norm((x @ wq.t()).view(B, H, hd), L["q_norm"]))
+        k = rope(norm((x @ wk.t()).view(B, KV, hd), L["k_norm"]))
+        v = (x @ wv.t()).view(B, KV, hd)
         kc = torch.cat([f(caches[l][0][:, :, :pos]), k[:, :, None]], 2)
         vc = torch.cat([f(caches[l][1][:, :, :pos]), v[:, :, None]], 2)
         rep = H // KV
@@ -72,9 +73,10 @@ def _ref_step(dec: Decoder, caches, tokens, pos, expert_seed=1000):
     return norm(h, dec.final_norm) @ f(dec.lm_head).t()
 
 
-def test_decoder_step_matches_fp32_restatement(cuda):
+@pytest.mark.parametrize("fused", [True, False])
+def test_decoder_step_matches_fp32_restatement(cuda, fused):
     B, ctx = 3, 20
-    dec = Decoder(SMALL, B, ctx, max_steps=4, seed=3)
+    dec = Decoder(SMALL, B, ctx, max_steps=4, seed=3, fused=fused)
     caches = [(L["k_cache"].clone(), L["v_cache"].clone()) for L in dec.layers]
     toks = torch.tensor([5, 77, 300], device=cuda)
     eager = dec.step(toks).float().clone()
@@ -97,3 +99,24 @@ def test_graph_replay_equals_eager(cuda):
         assert torch.equal(la, lb)
         toks = la.argmax(-1)
     assert int(a.pos) == int(b.pos) == ctx + 3
+
+
+def test_fused_step_matches_unfused(cuda):
+    """The fused kernels (add + RMS norm, q/k norm + rotary + cache write,
+    one q|k|v GEMM) round at the same points as the torch ops they replace:
+    logits and the written cache rows agree to a few bf16 ulps."""
+    B, ctx = 3, 20
+    a = Decoder(SMALL, B, ctx, max_steps=4, seed=5, fused=True)
+    b = Decoder(SMALL, B, ctx, max_steps=4, seed=5, fused=False)
+    toks = torch.tensor([9, 100, 511], device=cuda)
+    for _ in range(2):
+        la = a.step(toks).float().clone()
+        lb = b.step(toks).float().clone()
+        rms = float(lb.pow(2).mean().sqrt())
+        assert float((la - lb).abs().max()) <= 1e-2 * rms
+        toks = lb.argmax(-1)
+    for La, Lb in zip(a.layers, b.layers):
+        for name in ("k_cache", "v_cache"):
+            x, y = La[name][:, :, ctx:ctx + 2].float(), Lb[name][:, :, ctx:ctx + 2].float()
+            assert float((x - y).abs().max()) <= 2e-2 * float(y.pow(2).mean().sqrt())
+            assert torch.equal(La[name][:, :, :ctx], Lb[name][:, :, :ctx])
