@@ -211,7 +211,7 @@ def measure_prefill(T, steps, warmup, layers=2):
     captured; CUDA events on the launching stream."""
     import torch
     from expert_sniper_b200 import MoEBlock, PRESETS
-    from expert_sniper_b200.block import uses_tensor_path
+    from expert_sniper_b200.block import ffn_kernels
     from expert_sniper_b200.quant import synthetic_inputs, synthetic_layer
 
     cfg = PRESETS["qwen3-next-80b-a3b"]
@@ -292,7 +292,7 @@ def measure_prefill(T, steps, warmup, layers=2):
     dom = max(["gateup", "down"], key=lambda n: kmean[n])
     return {
         "metric": PREFILL_METRIC, "value": T / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms,
-        "steps": steps, "tokens": T, "kernel_path": "tensor" if uses_tensor_path(cfg, T) else "decode",
+        "steps": steps, "tokens": T, "kernel_path": ffn_kernels(cfg, T),
         "config": {"workload": f"{cfg.name} MoE layer prefill, {T} tokens, no routing bias, "
                                f"{layers} alternating layers of {cfg.packed_bytes / 1e6:.0f} MB",
                    "model": cfg.name, "hidden": D, "experts": cfg.num_experts, "top_k": k,

@@ -81,11 +81,23 @@ def prepare_packed(cfg: MoEConfig, weights: dict, out: torch.Tensor = None) -> t
 def uses_tensor_path(cfg: MoEConfig, T: int) -> bool:
     """Whether a call with T tokens runs the tensor-core (tcgen05) expert
     kernels: the rule of es_moe_cfg.kernel_path in include/es_moe.h."""
-    if cfg.x_dtype == "f16":
-        return True
+    return ffn_kernels(cfg, T) != "decode"
+
+
+def ffn_kernels(cfg: MoEConfig, T: int) -> str:
+    """The expert-FFN kernels a call with T tokens runs ("decode", "tensor"
+    or "tensor-small"): the rule of es_moe_cfg.kernel_path in
+    include/es_moe.h (automatic: by the average pairs per routed expert
+    p = T k / E, decode below 8, 32-token tiles up to 24, 128-token tiles
+    above, tensor-core kernels only from T = 64)."""
     if cfg.kernel_path != "auto":
-        return cfg.kernel_path == "tensor"
-    return T >= 64 and T * cfg.top_k >= 16 * cfg.num_experts
+        return cfg.kernel_path
+    pk = T * cfg.top_k
+    if T >= 64 and pk >= 24 * cfg.num_experts:
+        return "tensor"
+    if T >= 64 and pk >= 8 * cfg.num_experts:
+        return "tensor-small"
+    return "tensor-small" if cfg.x_dtype == "f16" else "decode"
 
 
 class MoEBlock:
@@ -224,7 +236,7 @@ class MoEBlock:
                    out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor = None,
                    kernel_path: str = None):
         """Experts + combine for given routing (-1 ids are skipped).
-        `kernel_path` ("auto", "decode", "tensor") overrides the block's
+        `kernel_path` ("auto", "decode", "tensor", "tensor-small") overrides the block's
         config for this call (e.g. when most slots are masked, the caller
         knows the real number of pairs per expert better than the row count
         does)."""

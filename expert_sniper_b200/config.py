@@ -12,7 +12,7 @@ import ctypes
 from dataclasses import dataclass, replace
 
 
-KERNEL_PATHS = {"auto": 0, "decode": 1, "tensor": 2}
+KERNEL_PATHS = {"auto": 0, "decode": 1, "tensor": 2, "tensor-small": 3}
 X_DTYPES = {"bf16": 0, "f16": 1}  # es_dtype codes
 
 

@@ -26,21 +26,29 @@ es_status check_cfg(const es_moe_cfg* c) {
   if (c->num_experts > es::kMaxExperts) return ES_ERR_UNSUPPORTED;
   if (c->top_k > es::kMaxTopK) return ES_ERR_UNSUPPORTED;
   if (c->shared_inter != 0 && c->shared_inter != c->inter) return ES_ERR_UNSUPPORTED;
-  if (c->kernel_path < 0 || c->kernel_path > 2) return ES_ERR_INVALID_ARG;
+  if (c->kernel_path < 0 || c->kernel_path > 3) return ES_ERR_INVALID_ARG;
   if (c->x_dtype != ES_DTYPE_BF16 && c->x_dtype != ES_DTYPE_F16) return ES_ERR_UNSUPPORTED;
   // the decode kernels read bf16 activations only
   if (c->x_dtype == ES_DTYPE_F16 && c->kernel_path == 1) return ES_ERR_UNSUPPORTED;
   return ES_OK;
 }
 
-// Tensor-core (tcgen05) expert FFN for batches that give each routed expert
-// enough tokens to fill an MMA tile; the register-operand decode kernels
-// otherwise.
-bool use_tensor_cores(const es_moe_cfg* c, int T) {
-  if (c->x_dtype == ES_DTYPE_F16) return true;
-  if (c->kernel_path == 1) return false;
-  if (c->kernel_path == 2) return true;
-  return T >= 64 && (long long)T * c->top_k >= 16LL * c->num_experts;
+// Which expert-FFN kernels run: 0 = the register-operand decode kernels,
+// 1 = tensor-core GEMMs with 128-token tiles (A in shared memory), 2 = tensor-
+// core GEMMs with 32-token tiles (A in tensor memory). Automatic, by the
+// average (token, expert) pairs per routed expert p = T k / E (and T >= 64):
+// decode below p = 8, 32-token tiles up to p = 24, 128-token tiles above --
+// the crossovers measured on a B200 for the Qwen3-30B and Qwen3-Next layers.
+enum { kFfnDecode = 0, kFfnTensorLarge = 1, kFfnTensorSmall = 2 };
+int ffn_variant(const es_moe_cfg* c, int T) {
+  if (c->kernel_path == 3) return kFfnTensorSmall;
+  if (c->kernel_path == 2) return kFfnTensorLarge;
+  if (c->kernel_path == 1) return kFfnDecode;  // (fp16 x is rejected with path 1)
+  const long long pk = (long long)T * c->top_k;
+  if (T >= 64 && pk >= 24LL * c->num_experts) return kFfnTensorLarge;
+  if (T >= 64 && pk >= 8LL * c->num_experts) return kFfnTensorSmall;
+  // fp16 activations are read by the tensor-core kernels only
+  return c->x_dtype == ES_DTYPE_F16 ? kFfnTensorSmall : kFfnDecode;
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -107,10 +115,11 @@ es_status run_pf_front(const es_moe_cfg* cfg, const Workspace& w, const es::Rout
 
 // Tensor-core path: grouped GEMMs (gate/up, down) and the fp16-row combine.
 es_status run_pf_ffn(const es_moe_cfg* cfg, const Workspace& w, const void* packed, void* out,
-                     int out_f32, int T, cudaStream_t st, const Marks& mk) {
+                     int out_f32, int T, bool small, cudaStream_t st, const Marks& mk) {
   const int E1 = cfg->num_experts + (cfg->shared_inter > 0 ? 1 : 0);
   const long long pairs = (long long)T * w.kk;
-  const long long tiles = pairs / 128 + (pairs < E1 ? pairs : E1);  // >= sum of ceil(n_e / 128)
+  const int nt = small ? es::kSmallTile : es::kLargeTile;
+  const long long tiles = pairs / nt + (pairs < E1 ? pairs : E1);  // >= sum of ceil(n_e / nt)
   es::PfArgs a{};
   a.packed = static_cast<const uint8_t*>(packed);
   a.expert_bytes = es::expert_bytes(cfg->hidden, cfg->inter);
@@ -122,9 +131,9 @@ es_status run_pf_ffn(const es_moe_cfg* cfg, const Workspace& w, const void* pack
   const int gu_max = gu_units > (1 << 30) ? (1 << 30) : (int)gu_units;
   const int dn_max = dn_units > (1 << 30) ? (1 << 30) : (int)dn_units;
   if (mk.mark(2, st) != cudaSuccess) return ES_ERR_CUDA;
-  if (es::launch_pf_gateup(a, T, gu_max, st) != cudaSuccess) return ES_ERR_CUDA;
+  if (es::launch_pf_gateup(a, T, gu_max, small, st) != cudaSuccess) return ES_ERR_CUDA;
   if (mk.mark(3, st) != cudaSuccess) return ES_ERR_CUDA;
-  if (es::launch_pf_down(a, (long long)w.P, dn_max, st) != cudaSuccess) return ES_ERR_CUDA;
+  if (es::launch_pf_down(a, (long long)w.P, dn_max, small, st) != cudaSuccess) return ES_ERR_CUDA;
   if (mk.mark(4, st) != cudaSuccess) return ES_ERR_CUDA;
   es::CombineArgs cb{};
   cb.cs_pos = w.cs_pos; cb.cs_w = w.cs_w; cb.pos_shared = w.pos; cb.sgate = w.sgate;
@@ -332,11 +341,13 @@ es_status es_moe_expert_ffn(const es_moe_cfg* cfg, const void* x, const int32_t*
   r.x_f16 = cfg->x_dtype == ES_DTYPE_F16;
   r.sgate = w.sgate; r.x_perm = w.x_perm; r.xsum = w.xsum; r.err = w.err;
   Marks mk;
-  if (use_tensor_cores(cfg, T)) {
+  const int v = ffn_variant(cfg, T);
+  if (v != kFfnDecode) {
     r.out_idx = nullptr; r.out_w = nullptr;
     es_status s2 = run_pf_front(cfg, w, r, T, st, mk);
     if (s2 != ES_OK) return s2;
-    return run_pf_ffn(cfg, w, packed, out, out_dtype == ES_DTYPE_F32, T, st, mk);
+    return run_pf_ffn(cfg, w, packed, out, out_dtype == ES_DTYPE_F32, T, v == kFfnTensorSmall,
+                      st, mk);
   }
   es_status s2 = run_front(cfg, w, r, topk_idx, topk_w, T, st, mk);
   if (s2 != ES_OK) return s2;
@@ -380,10 +391,12 @@ es_status es_moe_forward_timed(const es_moe_cfg* cfg, const void* x, const void*
   r.x_f16 = cfg->x_dtype == ES_DTYPE_F16;
   r.out_idx = idx; r.out_w = wts;
   r.sgate = w.sgate; r.x_perm = w.x_perm; r.xsum = w.xsum; r.err = w.err;
-  if (use_tensor_cores(cfg, T)) {
+  const int v = ffn_variant(cfg, T);
+  if (v != kFfnDecode) {
     es_status s2 = run_pf_front(cfg, w, r, T, st, mk);
     if (s2 != ES_OK) return s2;
-    return run_pf_ffn(cfg, w, packed, out, out_dtype == ES_DTYPE_F32, T, st, mk);
+    return run_pf_ffn(cfg, w, packed, out, out_dtype == ES_DTYPE_F32, T, v == kFfnTensorSmall,
+                      st, mk);
   }
   es_status s2 = run_front(cfg, w, r, idx, wts, T, st, mk);
   if (s2 != ES_OK) return s2;

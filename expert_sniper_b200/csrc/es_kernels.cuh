@@ -171,8 +171,14 @@ cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st);
 // tensor-core path
 cudaError_t launch_pf_front(const RouteArgs& r, const PfFrontArgs& d, cudaStream_t st);
 cudaError_t launch_pf_scatter(const PfScatterArgs& a, cudaStream_t st);
-cudaError_t launch_pf_gateup(const PfArgs& a, long long tokens, int max_units, cudaStream_t st);
-cudaError_t launch_pf_down(const PfArgs& a, long long pairs, int max_units, cudaStream_t st);
+// token tiles of the tensor-core GEMMs: large batches (A in shared memory)
+// and small ones (A in tensor memory)
+constexpr int kLargeTile = 128;
+constexpr int kSmallTile = 32;
+cudaError_t launch_pf_gateup(const PfArgs& a, long long tokens, int max_units, bool small,
+                             cudaStream_t st);
+cudaError_t launch_pf_down(const PfArgs& a, long long pairs, int max_units, bool small,
+                           cudaStream_t st);
 cudaError_t launch_prepare(const PrepareArgs& a, cudaStream_t st);
 
 }  // namespace es

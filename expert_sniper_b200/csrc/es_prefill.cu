@@ -85,6 +85,34 @@ ES_DEV void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t i
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T: A is read from tensor memory (lane = row
+// of A, each 32-bit column two consecutive K elements), B from shared memory
+ES_DEV void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                        uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 TMEM lanes x 32 consecutive 32-bit columns from registers: thread i of
+// the warp writes lane (base lane + i), columns col .. col + 31
+ES_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+// waits until this thread's tcgen05.st writes are done
+ES_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+
 // mbarrier arrives once every tcgen05 op issued so far by this thread is done
 ES_DEV void umma_commit(uint64_t* bar) {
   asm volatile(
@@ -127,6 +155,7 @@ ES_DEV void cp_async_arrive(uint64_t* bar) {
                : "memory");
 }
 ES_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 
 // generic-proxy writes to shared memory -> visible to the tensor core's reads
 ES_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
@@ -353,32 +382,48 @@ __global__ void __launch_bounds__(256) pf_scatter_kernel(PfScatterArgs a) {
 // ---------------------------------------------------------------------------
 // Grouped GEMM
 // ---------------------------------------------------------------------------
-constexpr int kNT = 128;          // token tile (UMMA N, at most)
 constexpr int kM = 128;           // weight rows per unit (UMMA M)
 constexpr int kThreads = 768;
 constexpr int kNumBThreads = 64;  // warps 2-3 (gate/up: cp.async gathers)
 constexpr int kWarpLoad = 0, kWarpMma = 1, kWarpB = 2, kWarpEpi0 = 4, kWarpDq0 = 8,
-              kNumDqWarps = 8,   // one 16-row block each, per K-block
-              kDqGroups = 2;     // groups of kNumDqWarps, alternating K-blocks
+              kDqWarps = 16;     // warps 8-23
 constexpr int kRun = 4 * kTileBytes;  // four contiguous 576-byte tiles
 
+// Two variants of the GEMM:
+//   TA = false (large batches): token tiles of NT = 128; A is dequantised
+//     into 128-byte-swizzled shared memory by eight warps per K-block (one
+//     16-row block each), two groups taking alternate K-blocks;
+//   TA = true (small batches): token tiles of NT = 32; A is dequantised
+//     into TENSOR MEMORY (tcgen05.st, one weight row per thread: four warps,
+//     one per TMEM lane quarter, per K-block; four groups taking K-blocks in
+//     turn) and the MMA reads it from there, so no fp16 weights pass
+//     through shared memory.
 // Rings: raw code tiles (bulk copies, HBM latency) and operand slots, each
 // holding one K-block of A (dequantised weights, written by the dequant
 // warps) and of B (activation rows), completed on one barrier.
-template <bool GU>
+template <bool GU, int NT, bool TA>
 struct PfCfg {
   static constexpr int kProj = GU ? 2 : 1;
   static constexpr int kTiles = 8 * kProj;  // 16-row tiles per K-block
   static constexpr int kRawBytes = kTiles * kTileBytes;
-  static constexpr int kABytes = kM * 128;  // one projection
-  static constexpr int kAStage = kProj * kABytes;
-  static constexpr int kBStage = kNT * 128;
-  static constexpr int kRawStages = GU ? 3 : 6;
-  static constexpr int kOpStages = GU ? 4 : 6;  // A and B share slots and barriers
-  static constexpr int kAccCols = kProj * kNT;
-  static constexpr int kTmemCols = 2 * kAccCols;  // two accumulator buffers
-  static constexpr size_t kSmem = 1024 + (size_t)kOpStages * (kAStage + kBStage) +
-                                  (size_t)kRawStages * kRawBytes;
+  static constexpr int kABytes = kM * 128;  // one projection (shared-memory A)
+  static constexpr int kAStage = TA ? 0 : kProj * kABytes;
+  static constexpr int kBStage = NT * 128;
+  static constexpr int kRawStages = TA ? 8 : (GU ? 3 : 6);
+  static constexpr int kOpStages = TA ? (GU ? 6 : 8) : (GU ? 4 : 6);  // A and B share barriers
+  static constexpr int kNumDqWarps = TA ? 4 : 8;                 // warps per K-block
+  static constexpr int kDqGroups = kDqWarps / kNumDqWarps;       // take K-blocks in turn
+  static constexpr size_t kRawRing = (size_t)kRawStages * kRawBytes;
+  static constexpr int kAccCols = kProj * NT;
+  static constexpr int kACols = TA ? kProj * (kGroup / 2) : 0;   // TMEM A columns per slot
+  static constexpr int kTmemCols = TA ? 512 : 2 * kAccCols;      // power of two >= 32
+  static_assert(2 * kAccCols + kOpStages * kACols <= kTmemCols, "tensor memory budget");
+  static_assert(NT % 32 == 0 && NT <= 128, "token tile");
+  // the small-batch variant needs little shared memory; ask for more than
+  // half an SM's so that one CTA (and one 512-column TMEM allocation) runs
+  // per SM
+  static constexpr size_t kSmemNeed = 1024 + (size_t)kOpStages * (kAStage + kBStage) + kRawRing;
+  static constexpr size_t kSmem = (TA && kSmemNeed < 120 * 1024) ? 120 * 1024 : kSmemNeed;
 };
 
 ES_DEV void tma_tile2d(void* dst, const CUtensorMap* tm, int col, int row, uint64_t* bar) {
@@ -412,8 +457,9 @@ ES_DEV bool warp_wait(uint64_t* bar, uint32_t phase) {
   return __shfl_sync(0xffffffffu, ok, 0);
 }
 
-// unit u -> (expert, row block, token tile); s_ts = tile prefix over the
-// active list (n_act + 1 entries)
+// unit u -> (expert, row block, token tile of NT); s_ts = tile prefix over
+// the active list (n_act + 1 entries)
+template <int NT>
 ES_DEV Unit decode_unit(const PfArgs& a, const int* s_ts, int n_act, int RB, int u) {
   const int t = u / RB;
   Unit r;
@@ -425,9 +471,9 @@ ES_DEV Unit decode_unit(const PfArgs& a, const int* s_ts, int n_act, int RB, int
   }
   const int ti = t - s_ts[lo];
   r.e = a.act_e[lo];
-  r.pair0 = a.act_off[lo] + ti * kNT;
-  const int rem = a.act_n[lo] - ti * kNT;
-  r.n = rem < kNT ? rem : kNT;
+  r.pair0 = a.act_off[lo] + ti * NT;
+  const int rem = a.act_n[lo] - ti * NT;
+  r.n = rem < NT ? rem : NT;
   return r;
 }
 
@@ -455,9 +501,10 @@ ES_DEV void drain_ring(uint64_t* full, int stages, int q, uint32_t* err) {
     }
 }
 
-template <bool GU>
+template <bool GU, int NT, bool TA>
 __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_constant__ PfArgs a) {
-  using C = PfCfg<GU>;
+  using C = PfCfg<GU, NT, TA>;
+  constexpr int kNT = NT;
   extern __shared__ uint8_t dsmem[];
   __shared__ __align__(8) uint64_t raw_full[C::kRawStages], raw_empty[C::kRawStages];
   __shared__ __align__(8) uint64_t op_full[C::kOpStages], op_empty[C::kOpStages];
@@ -479,12 +526,12 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
   if (tid == 0) {
     for (int i = 0; i < C::kRawStages; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], kNumDqWarps);
+      mbar_init(&raw_empty[i], C::kNumDqWarps);
     }
     for (int i = 0; i < C::kOpStages; ++i) {
       // full: the 8 dequant warps of a K-block plus its B rows (64 cp.async
       // threads for gate/up, one TMA arrival for down); empty: the MMA commit
-      mbar_init(&op_full[i], kNumDqWarps + (GU ? kNumBThreads : 1));
+      mbar_init(&op_full[i], C::kNumDqWarps + (GU ? kNumBThreads : 1));
       mbar_init(&op_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -553,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
       int q = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const Unit un = decode_unit(a, s_ts, n_act, RB, u);
+        const Unit un = decode_unit<NT>(a, s_ts, n_act, RB, u);
         const uint8_t* eb = a.packed + (size_t)un.e * a.expert_bytes;
         for (int kb = 0; kb < KB; ++kb, ++q) {
           const int s = q % C::kRawStages;
@@ -584,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
     uint32_t ph = 0;  // operand ring slot and its phase parity
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++iu) {
-      const Unit un = decode_unit(a, s_ts, n_act, RB, u);
+      const Unit un = decode_unit<NT>(a, s_ts, n_act, RB, u);
       const uint32_t idesc = idesc_f16_m128((un.n + 15) & ~15);
       const int buf = iu & 1;
       if (!warp_wait(&acc_empty[buf], ((iu >> 1) & 1) ^ 1)) {
@@ -602,19 +649,34 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
           break;
         }
         tc_fence_after();
-        const uint64_t adesc0 = sw128_desc(sa + (size_t)so * C::kAStage);
         const uint64_t bdesc = sw128_desc(sb + (size_t)so * C::kBStage);
-        if (elect_one()) {
+        if (TA) {
+          // A slot so: columns [2 kAccCols + so kACols, + kACols), 32 per
+          // projection, 8 per K = 16 step
+          const uint32_t a0 = tmem + 2 * C::kAccCols + so * C::kACols;
+          if (elect_one()) {
 #pragma unroll
-          for (int pj = 0; pj < C::kProj; ++pj) {
-            // projection pj's tile starts kABytes (16 KB = 1024 descriptor units) later
-            const uint64_t adesc = adesc0 + (uint64_t)pj * (C::kABytes >> 4);
+            for (int pj = 0; pj < C::kProj; ++pj)
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)  // K = 16 per instruction: +32 bytes
-              umma_f16(d0 + pj * kNT, adesc + 2 * kk, bdesc + 2 * kk, idesc,
-                       (kb > 0 || kk > 0) ? 1u : 0u);
+              for (int kk = 0; kk < 4; ++kk)
+                umma_f16_ts(d0 + pj * kNT, a0 + pj * (kGroup / 2) + 8 * kk, bdesc + 2 * kk, idesc,
+                            (kb > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&op_empty[so]);
           }
-          umma_commit(&op_empty[so]);
+        } else {
+          const uint64_t adesc0 = sw128_desc(sa + (size_t)so * C::kAStage);
+          if (elect_one()) {
+#pragma unroll
+            for (int pj = 0; pj < C::kProj; ++pj) {
+              // projection pj's tile starts kABytes (16 KB = 1024 descriptor units) later
+              const uint64_t adesc = adesc0 + (uint64_t)pj * (C::kABytes >> 4);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)  // K = 16 per instruction: +32 bytes
+                umma_f16(d0 + pj * kNT, adesc + 2 * kk, bdesc + 2 * kk, idesc,
+                         (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(&op_empty[so]);
+          }
         }
         __syncwarp();
         if (++so == C::kOpStages) { so = 0; ph ^= 1u; }
@@ -624,6 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
       __syncwarp();
     }
     if (!ok && lane == 0) { set_error(a.err, 0x8u); set_abort(); }
+    __syncwarp();  // elect.sync needs the whole warp converged
     if (elect_one()) umma_commit(&mma_done);
     __syncwarp();
     warp_wait(&mma_done, 0);
@@ -638,7 +701,7 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
       // its copies
       const int bt = tid - kWarpB * 32, ch = bt & 7, r0 = bt >> 3;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const Unit un = decode_unit(a, s_ts, n_act, RB, u);
+        const Unit un = decode_unit<NT>(a, s_ts, n_act, RB, u);
         const uint16_t* rows[kNT / 8];
 #pragma unroll
         for (int i = 0; i < kNT / 8; ++i) {
@@ -667,7 +730,7 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
     } else if (warp == kWarpB) {
       // 128 consecutive pair rows of h16: one TMA tile per K-block
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const Unit un = decode_unit(a, s_ts, n_act, RB, u);
+        const Unit un = decode_unit<NT>(a, s_ts, n_act, RB, u);
         for (int kb = 0; kb < KB; ++kb, ++q) {
           const int s = q % C::kOpStages;
           if (!warp_wait(&op_empty[s], ((q / C::kOpStages) & 1) ^ 1)) {
@@ -693,7 +756,7 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
     bool ok = true;
     uint32_t range_err = 0;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++iu) {
-      const Unit un = decode_unit(a, s_ts, n_act, RB, u);
+      const Unit un = decode_unit<NT>(a, s_ts, n_act, RB, u);
       const int buf = iu & 1;
       // inverse token scales: lane holds tokens lane + 32 i, shuffled out per column
       float inv_r[kNT / 32];
@@ -713,7 +776,10 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
       for (int j0 = 0; j0 < npad; j0 += 16) {
         if (GU) {
           const int sel = j0 >> 5;
-          const float inv_sel = sel == 0 ? inv_r[0] : sel == 1 ? inv_r[1] : sel == 2 ? inv_r[2] : inv_r[3];
+          float inv_sel = inv_r[0];
+#pragma unroll
+          for (int i = 1; i < kNT / 32; ++i)
+            if (sel == i) inv_sel = inv_r[i];
           uint32_t g[16], v[16];
           tmem_ld16(tb + j0, g);
           tmem_ld16(tb + kNT + j0, v);
@@ -754,16 +820,78 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
     }
     if (range_err) set_error(a.err, 0x10u);
     if (!ok) { if (lane == 0) set_error(a.err, 0x8u); set_abort(); }
-  } else if (warp >= kWarpDq0) {
-    // ---------------- codes -> fp16 A tiles ----------------
-    const int dw = (warp - kWarpDq0) % kNumDqWarps;  // 16-row block of the unit
-    const int grp = (warp - kWarpDq0) / kNumDqWarps;  // takes K-blocks q = grp mod kDqGroups
+  } else if (TA && warp >= kWarpDq0) {
+    // ---------------- codes -> fp16 A in tensor memory ----------------
+    // warp (8 + 4 grp + dw): TMEM lane quarter dw (warp % 4), so thread
+    // `lane` owns weight row r = 32 dw + lane of the unit; group grp takes
+    // K-blocks q = grp mod kDqGroups
+    const int dw = (warp - kWarpDq0) % C::kNumDqWarps;
+    const int grp = (warp - kWarpDq0) / C::kNumDqWarps;
+    const int b16 = 2 * dw + (lane >> 4);  // 16-row tile of the row
+    const int g = lane & 7, hf = (lane >> 3) & 1;  // row g + 8 hf of that tile
+    const uint32_t a_lane = tmem + ((uint32_t)(32 * dw) << 16) + 2 * C::kAccCols;
+    int q = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      for (int kb = 0; kb < KB; ++kb, ++q) {
+        if (q % C::kDqGroups != grp) continue;
+        const int sr = q % C::kRawStages, s_a = q % C::kOpStages;
+        if (!warp_wait(&raw_full[sr], (q / C::kRawStages) & 1)) {
+          if (lane == 0) note_timeout(a.err, 7, q);
+          ok = false;
+          break;
+        }
+        // the row's eight code words (words 2c, 2c+1 sit in lane 4g + c's
+        // 16 bytes, row g + 8 in the upper half) and its (scale, bias)
+        uint2 wv[C::kProj][4];
+        uint32_t sbw[C::kProj];
+#pragma unroll
+        for (int pj = 0; pj < C::kProj; ++pj) {
+          const uint8_t* tile = raw + (size_t)sr * C::kRawBytes + (b16 * C::kProj + pj) * kTileBytes;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) wv[pj][c] = ld_shared8(tile + (4 * g + c) * 16 + hf * 8);
+          sbw[pj] = *reinterpret_cast<const uint32_t*>(tile + kTileCodeBytes + 8 * g + 4 * hf);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[sr]);
+        if (!warp_wait(&op_empty[s_a], ((q / C::kOpStages) & 1) ^ 1)) {
+          if (lane == 0) note_timeout(a.err, 8, q);
+          ok = false;
+          break;
+        }
+        if (aborted()) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int pj = 0; pj < C::kProj; ++pj) {
+          const __half2 s2 = __half2half2(__ushort_as_half((uint16_t)(sbw[pj] & 0xffffu)));
+          const __half2 b2 = __half2half2(__ushort_as_half((uint16_t)(sbw[pj] >> 16)));
+          uint32_t r[32];  // column 4j + s: elements (8j + s, 8j + s + 4), nibble order
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 o0 = dequant_word(wv[pj][c].x, s2, b2);
+            const uint4 o1 = dequant_word(wv[pj][c].y, s2, b2);
+            r[8 * c + 0] = o0.x; r[8 * c + 1] = o0.y; r[8 * c + 2] = o0.z; r[8 * c + 3] = o0.w;
+            r[8 * c + 4] = o1.x; r[8 * c + 5] = o1.y; r[8 * c + 6] = o1.z; r[8 * c + 7] = o1.w;
+          }
+          tmem_st32(a_lane + s_a * C::kACols + pj * (kGroup / 2), r);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&op_full[s_a]);
+      }
+    }
+    if (!ok) { if (lane == 0) set_error(a.err, 0x8u); set_abort(); }
+  } else if (!TA && warp >= kWarpDq0) {
+    // ---------------- codes -> fp16 A tiles in shared memory ----------------
+    const int dw = (warp - kWarpDq0) % C::kNumDqWarps;  // 16-row block of the unit
+    const int grp = (warp - kWarpDq0) / C::kNumDqWarps;  // takes K-blocks q = grp mod kDqGroups
     const int g = lane >> 2, c = lane & 3;
     int q = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
       for (int kb = 0; kb < KB; ++kb, ++q) {
-        if (q % kDqGroups != grp) continue;
+        if (q % C::kDqGroups != grp) continue;
         const int sr = q % C::kRawStages, s_a = q % C::kOpStages;
         if (!warp_wait(&raw_full[sr], (q / C::kRawStages) & 1)) {
           if (lane == 0) note_timeout(a.err, 7, q);
@@ -847,22 +975,22 @@ cudaError_t encode_rows_f16(CUtensorMap* m, const void* base, int cols, long lon
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <bool GU>
+template <bool GU, int NT, bool TA>
 cudaError_t launch_pf_gemm(const PfArgs& a_in, long long b_rows, int max_units,
                            cudaStream_t st) {
-  using C = PfCfg<GU>;
+  using C = PfCfg<GU, NT, TA>;
   int grid = sm_count();
   if (max_units < grid) grid = max_units;
   if (grid <= 0) return cudaSuccess;
   PfArgs a = a_in;
   // down loads 128 consecutive pair rows of h16 per TMA tile; gate/up
   // gathers token rows with cp.async and needs no tensor map
-  cudaError_t e = GU ? cudaSuccess : encode_rows_f16(&a.tm_b, a.h16, a.I, b_rows, kNT);
+  cudaError_t e = GU ? cudaSuccess : encode_rows_f16(&a.tm_b, a.h16, a.I, b_rows, NT);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(pf_gemm_kernel<GU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)C::kSmem);
+  e = cudaFuncSetAttribute(pf_gemm_kernel<GU, NT, TA>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
   if (e != cudaSuccess) return e;
-  return launch_pdl(pf_gemm_kernel<GU>, dim3(grid), dim3(kThreads), C::kSmem, st, a);
+  return launch_pdl(pf_gemm_kernel<GU, NT, TA>, dim3(grid), dim3(kThreads), C::kSmem, st, a);
 }
 
 template <int VPL>
@@ -892,12 +1020,16 @@ cudaError_t launch_pf_scatter(const PfScatterArgs& a, cudaStream_t st) {
   return launch_pdl(pf_scatter_kernel, dim3((n + 255) / 256), dim3(256), 0, st, a);
 }
 
-cudaError_t launch_pf_gateup(const PfArgs& a, long long tokens, int max_units, cudaStream_t st) {
-  return launch_pf_gemm<true>(a, tokens, max_units, st);
+cudaError_t launch_pf_gateup(const PfArgs& a, long long tokens, int max_units, bool small,
+                             cudaStream_t st) {
+  return small ? launch_pf_gemm<true, kSmallTile, true>(a, tokens, max_units, st)
+               : launch_pf_gemm<true, kLargeTile, false>(a, tokens, max_units, st);
 }
 
-cudaError_t launch_pf_down(const PfArgs& a, long long pairs, int max_units, cudaStream_t st) {
-  return launch_pf_gemm<false>(a, pairs, max_units, st);
+cudaError_t launch_pf_down(const PfArgs& a, long long pairs, int max_units, bool small,
+                           cudaStream_t st) {
+  return small ? launch_pf_gemm<false, kSmallTile, true>(a, pairs, max_units, st)
+               : launch_pf_gemm<false, kLargeTile, false>(a, pairs, max_units, st);
 }
 
 }  // namespace es

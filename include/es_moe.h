@@ -79,20 +79,24 @@ typedef struct es_moe_cfg {
   int32_t kernel_path;    /* which expert-FFN kernels run (no reference
                            * counterpart; results agree within the parity
                            * tolerance either way):
-                           *   0 = automatic: the tensor-core path when the
-                           *       batch gives the routed experts at least
-                           *       16 (token, expert) pairs each on average
-                           *       (T * top_k >= 16 * num_experts) and
-                           *       T >= 64, the decode path otherwise;
+                           *   0 = automatic, by the average (token,
+                           *       expert) pairs per routed expert
+                           *       p = T * top_k / num_experts: with
+                           *       T >= 64, path 2 for p >= 24, path 3 for
+                           *       8 <= p < 24; the decode path otherwise
+                           *       (path 3 for fp16 x);
                            *   1 = decode path (register-operand GEMV on the
                            *       4-bit codes, fp32 per-pair rows);
                            *   2 = tensor-core path (tcgen05 grouped GEMM,
                            *       fp16 operands dequantised in shared
-                           *       memory, fp16 per-pair rows)              */
+                           *       memory, fp16 per-pair rows);
+                           *   3 = tensor-core path with 32-token tiles and
+                           *       the dequantised weights in tensor memory
+                           *       (same arithmetic as 2)                    */
   int32_t x_dtype;        /* activations x: ES_DTYPE_BF16 (0, the model
                            * dtype) or ES_DTYPE_F16 (the Expert Network's
                            * wire dtype, protocol.py:3-9); fp16 x runs the
-                           * tensor-core path, which reads it without
+                           * tensor-core kernels, which read it without
                            * rounding (kernel_path 1 rejects it)            */
 } es_moe_cfg;
 

@@ -10,7 +10,9 @@ weights, h, down weights, y -- against the decode path's one).
 Cases cover several token tiles per expert, masked and duplicate slots,
 rows of very different magnitude, repeated calls (bitwise), agreement with
 the decode path, and the Qwen3-Next prefill and Qwen3-30B shapes at full
-size (sampled tokens against the oracle).
+size (sampled tokens against the oracle). Each runs on both variants of
+the GEMMs: "tensor" (128-token tiles, dequantised weights in shared memory)
+and "tensor-small" (32-token tiles, dequantised weights in tensor memory).
 """
 from __future__ import annotations
 
@@ -53,10 +55,14 @@ def _sample_check(out, x, idx, w_ref, lay_np, sg, rows, what):
     return err / rms
 
 
+PATHS = ["tensor", "tensor-small"]
+
+
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("T", [16, 64, 200])
 @pytest.mark.parametrize("bias", [False, True])
-def test_tensor_path_small(cuda, T, bias):
-    cfg = SMALL.with_(kernel_path="tensor")
+def test_tensor_path_small(cuda, T, bias, path):
+    cfg = SMALL.with_(kernel_path=path)
     lay, lay_np = _layer(cfg, 31, cuda)
     x, _, logits, sg = synthetic_inputs(cfg, T, seed=40 + T, device=cuda)
     cb = cache_bias_vector(cfg.num_experts, 0.5, T)[0].to(cuda) if bias else None
@@ -80,11 +86,12 @@ def test_tensor_path_small(cuda, T, bias):
     assert_close_rms(out.cpu().numpy(), dec.cpu().numpy(), rel=TENSOR_REL, what="vs decode")
 
 
-def test_tensor_path_many_tiles_masked_duplicates(cuda):
-    """Experts 0..3 in every token (T = 300: three 128-token tiles each),
-    masked slots (-1), a duplicated expert in one token, a token with
-    nothing routed."""
-    cfg = PLAIN.with_(kernel_path="tensor")
+@pytest.mark.parametrize("path", PATHS)
+def test_tensor_path_many_tiles_masked_duplicates(cuda, path):
+    """Experts 0..3 in every token (T = 300: three 128-token tiles each, or
+    ten 32-token tiles), masked slots (-1), a duplicated expert in one token,
+    a token with nothing routed."""
+    cfg = PLAIN.with_(kernel_path=path)
     lay, lay_np = _layer(cfg, 32, cuda)
     T = 300
     x, _, _, _ = synthetic_inputs(cfg, T, seed=5, device=cuda)
@@ -109,13 +116,14 @@ def test_tensor_path_many_tiles_masked_duplicates(cuda):
     assert torch.count_nonzero(out[9]) == 0
 
 
-def test_tensor_path_row_scales(cuda):
+@pytest.mark.parametrize("path", PATHS)
+def test_tensor_path_row_scales(cuda, path):
     """Rows scaled by 1e2 and 1e-1 against each row's own RMS: the
     activations' per-token power-of-two scale keeps every row's relative
     accuracy. (h and y are plain fp16 on both paths: much larger rows
     saturate h and are flagged, much smaller ones lose h to fp16 underflow;
     normalised hidden states stay far from both.)"""
-    cfg = PLAIN.with_(kernel_path="tensor")
+    cfg = PLAIN.with_(kernel_path=path)
     lay, lay_np = _layer(cfg, 32, cuda)
     T = 96
     x, _, logits, _ = synthetic_inputs(cfg, T, seed=6, device=cuda)
@@ -136,13 +144,18 @@ def test_tensor_path_row_scales(cuda):
         assert np.abs(o[t] - ref[t]).max() <= TENSOR_REL * rms, t
 
 
-@pytest.mark.parametrize("name,T,bias", [("qwen3-next-80b-a3b", 4096, False),
-                                         ("qwen3-30b-a3b", 512, True)])
-def test_tensor_path_full_shapes(cuda, name, T, bias):
-    """Full-size layers at prefill batch sizes (the automatic choice picks
-    the tensor path here); 64 sampled tokens against the oracle, all tokens
-    against the decode kernels."""
-    cfg = PRESETS[name]
+@pytest.mark.parametrize("name,T,bias,path", [("qwen3-next-80b-a3b", 4096, False, "auto"),
+                                              ("qwen3-30b-a3b", 512, True, "auto"),
+                                              ("qwen3-30b-a3b", 256, True, "auto"),
+                                              ("qwen3-30b-a3b", 64, True, "tensor-small"),
+                                              ("qwen3-30b-a3b", 1, True, "tensor-small"),
+                                              ("qwen3-next-80b-a3b", 8, False, "tensor-small")])
+def test_tensor_path_full_shapes(cuda, name, T, bias, path):
+    """Full-size layers: prefill batch sizes (the automatic choice picks the
+    tensor path there) and decode sizes on the small-tile variant; up to 64
+    sampled tokens against the oracle, all tokens against the decode
+    kernels."""
+    cfg = PRESETS[name].with_(kernel_path=path)
     lay, lay_np = _layer(cfg, 50, cuda)
     x, _, logits, sg = synthetic_inputs(cfg, T, seed=51, device=cuda)
     cb = cache_bias_vector(cfg.num_experts, 0.5, 3)[0].to(cuda) if bias else None
@@ -161,7 +174,7 @@ def test_tensor_path_full_shapes(cuda, name, T, bias):
     ok, _, _, bad = mo.topk_parity(idx_n, lg, cbn, cfg.top_k)
     assert ok, bad
     w_ref = oracle_weights_for(idx_n, lg, cbn, cfg.norm_topk_prob)
-    rows = np.random.default_rng(T).choice(T, 64, replace=False)
+    rows = np.random.default_rng(T).choice(T, min(T, 64), replace=False)
     rel = _sample_check(out.cpu().numpy(), x, idx_n, w_ref, lay_np, sg, rows, name)
     assert rel < TENSOR_REL
     dec = MoEBlock(cfg.with_(kernel_path="decode"), packed=blk.packed, shared_gate_w=sg,
