@@ -110,9 +110,11 @@ struct PfScatterArgs {
 // Grouped GEMM over (active expert, 128-row block, token tile) units.
 struct alignas(64) PfArgs {
   CUtensorMap tm_b;         // B rows: x16 (gate/up) or h16 (down); set by the launcher
+  CUtensorMap tm_a;         // packed code tiles (small-tile variant); set by the launcher
   const uint8_t* packed;
   size_t expert_bytes;
   int D, I;
+  int E1;                   // experts in the packed blob (routed + shared)
   const int32_t* n_active;
   const int32_t* act_e;
   const int32_t* act_off;

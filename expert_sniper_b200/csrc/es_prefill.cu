@@ -434,6 +434,19 @@ ES_DEV void tma_tile2d(void* dst, const CUtensorMap* tm, int col, int row, uint6
       : "memory");
 }
 
+// One K-block of a unit's code tiles (its 16-row tiles for one quantisation
+// group: runs of four contiguous 576-byte tiles, GD (or KG) runs apart) with
+// one 5-D TMA load: 8-byte elements, dims {144, 2, group, run, expert}, box
+// {144, 2, 1, runs, 1}, x coordinate 0; lands as the runs back to back.
+ES_DEV void tma_codes5d(void* dst, const CUtensorMap* tm, int group, int run0, int expert,
+                        uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;\n" ::"r"(smem_addr(dst)),
+      "l"(tm), "r"(0), "r"(0), "r"(group), "r"(run0), "r"(expert), "r"(smem_addr(bar)), "l"(pol)
+      : "memory");
+}
+
 struct Unit {
   int e, rb, pair0, n;
 };
@@ -612,11 +625,15 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
           if (aborted()) { ok = false; break; }
           mbar_arrive_expect_tx(&raw_full[s], C::kRawBytes);
           uint8_t* dst = raw + (size_t)s * C::kRawBytes;
+          if (TA) {
+            tma_codes5d(dst, &a.tm_a, kb, (C::kRawBytes / kRun) * un.rb, un.e, &raw_full[s], pol);
+          } else {
 #pragma unroll
-          for (int p = 0; p < C::kRawBytes / kRun; ++p) {
-            const size_t off = GU ? gateup_tile_off(GD, 2 * (un.rb * 4 + p), kb, 0)
-                                  : down_tile_off(a.D, a.I, 4 * (un.rb * 2 + p), kb);
-            bulk_copy_g2s(dst + p * kRun, eb + off, kRun, &raw_full[s], pol);
+            for (int p = 0; p < C::kRawBytes / kRun; ++p) {
+              const size_t off = GU ? gateup_tile_off(GD, 2 * (un.rb * 4 + p), kb, 0)
+                                    : down_tile_off(a.D, a.I, 4 * (un.rb * 2 + p), kb);
+              bulk_copy_g2s(dst + p * kRun, eb + off, kRun, &raw_full[s], pol);
+            }
           }
         }
       }
@@ -975,6 +992,28 @@ cudaError_t encode_rows_f16(CUtensorMap* m, const void* base, int cols, long lon
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// 5-D map of one projection region's code tiles, 8-byte elements:
+// {144, 2} = one 2304-byte run, then group (stride 2304 B), run (stride
+// groups x 2304 B), expert (stride expert_bytes); box {144, 2, 1, runs, 1}
+cudaError_t encode_codes_map(CUtensorMap* m, const PfArgs& a, bool gu, int runs) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  const int groups = (gu ? a.D : a.I) / kGroup;
+  const int nruns = gu ? a.I / 32 : a.D / 64;
+  const uint8_t* base = a.packed + (gu ? 0 : gateup_region_bytes(a.D, a.I));
+  const cuuint64_t dims[5] = {kRun / 16, 2, (cuuint64_t)groups, (cuuint64_t)nruns,
+                              (cuuint64_t)a.E1};
+  const cuuint64_t strides[4] = {kRun / 2, kRun, (cuuint64_t)groups * kRun,
+                                 (cuuint64_t)a.expert_bytes};
+  const cuuint32_t box[5] = {kRun / 16, 2, 1, (cuuint32_t)runs, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 5, const_cast<uint8_t*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 template <bool GU, int NT, bool TA>
 cudaError_t launch_pf_gemm(const PfArgs& a_in, long long b_rows, int max_units,
                            cudaStream_t st) {
@@ -987,6 +1026,11 @@ cudaError_t launch_pf_gemm(const PfArgs& a_in, long long b_rows, int max_units,
   // gathers token rows with cp.async and needs no tensor map
   cudaError_t e = GU ? cudaSuccess : encode_rows_f16(&a.tm_b, a.h16, a.I, b_rows, NT);
   if (e != cudaSuccess) return e;
+  if (TA) {
+    static_assert(C::kRawBytes % kRun == 0, "whole runs per K-block");
+    e = encode_codes_map(&a.tm_a, a, GU, C::kRawBytes / kRun);
+    if (e != cudaSuccess) return e;
+  }
   e = cudaFuncSetAttribute(pf_gemm_kernel<GU, NT, TA>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
   if (e != cudaSuccess) return e;

@@ -118,11 +118,11 @@ def test_config_validation_in_python():
 def test_automatic_kernel_choice():
     """The automatic expert-FFN kernel rule (es_moe_cfg.kernel_path 0), by
     average pairs per routed expert p = T k / E: decode below 8, 32-token
-    tensor tiles up to 24, 128-token tiles above; tensor kernels from T = 64;
+    tensor tiles up to 32, 128-token tiles above; tensor kernels from T = 64;
     fp16 activations never take the decode kernels."""
     from expert_sniper_b200.block import ffn_kernels, uses_tensor_path
     q = PRESETS["qwen3-30b-a3b"]          # E = 128, k = 8
-    assert [ffn_kernels(q, T) for T in (1, 8, 64, 127, 128, 256, 383, 384, 4096)] == [
+    assert [ffn_kernels(q, T) for T in (1, 8, 64, 127, 128, 256, 512, 513, 4096)] == [
         "decode", "decode", "decode", "decode", "tensor-small", "tensor-small", "tensor-small",
         "tensor", "tensor"]
     small = MoEConfig(256, 4, 2, 256, True)  # p = T / 2: the T >= 64 floor decides
