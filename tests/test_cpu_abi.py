@@ -126,7 +126,8 @@ def test_automatic_kernel_choice():
         "decode", "decode", "decode", "decode", "tensor-small", "tensor-small", "tensor-small",
         "tensor", "tensor"]
     small = MoEConfig(256, 4, 2, 256, True)  # p = T / 2: the T >= 64 floor decides
-    assert ffn_kernels(small, 32) == "decode" and ffn_kernels(small, 64) == "tensor"
+    assert ffn_kernels(small, 32) == "decode" and ffn_kernels(small, 64) == "tensor-small"
+    assert ffn_kernels(small, 66) == "tensor"
     f16 = q.with_(x_dtype="f16")
     assert ffn_kernels(f16, 8) == "tensor-small" and ffn_kernels(f16, 4096) == "tensor"
     for path in ("decode", "tensor", "tensor-small"):
