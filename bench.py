@@ -49,6 +49,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--kernel-path", default="auto",
+                    choices=["auto", "decode", "tensor", "tensor-small"],
+                    help="expert-FFN kernels of the decode line (es_moe_cfg.kernel_path)")
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--sweep", default="1,8", help="extra decode batch sizes to time (\"\" for none)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -145,21 +148,26 @@ def block_bytes(cfg, T, U):
             + cfg.num_experts * 4)
 
 
-def kernel_bytes(cfg, T, U):
-    """Algorithmic bytes per launch of each kernel of the block."""
+def kernel_bytes(cfg, T, U, path="decode"):
+    """Algorithmic bytes per launch of each kernel of the block. `path` is
+    the expert-FFN kernels that ran: the decode kernels keep per-pair rows
+    in fp32 and x as bf16 fragments plus 64-column sums; the tensor-core
+    kernels keep fp16 rows and x as scaled fp16 with one scale per token."""
     D, I, E, k = cfg.hidden, cfg.inter, cfg.num_experts, cfg.top_k
     P = T * k
+    yb = 4 if path == "decode" else 2
+    xprep = T * D * 2 + (T * (D // 64) * 4 if path == "decode" else T * 4)
     return {
-        # router + dispatch + operand prep: logits, bias, x in, x_perm + sums out,
+        # router + dispatch + operand prep: logits, bias, x in, prepared x out,
         # routing lists out
-        "front": T * E * 2 + E * 4 + T * D * 2 * 2 + T * (D // 64) * 4 + 3 * T * k * 8 + E * 16,
+        "front": T * E * 2 + E * 4 + T * D * 2 + xprep + 3 * T * k * 8 + E * 16,
         "gap": 0,
-        # packed gate+up tiles of the distinct experts, x_perm in, fp16 h out
+        # packed gate+up tiles of the distinct experts, prepared x in, fp16 h out
         "gateup": U * 2 * D * I * 9 // 16 + T * D * 2 + P * I * 2,
-        # packed down tiles, fp16 h in, fp32 per-pair rows out
-        "down": U * D * I * 9 // 16 + P * I * 2 + P * D * 4,
+        # packed down tiles, fp16 h in, per-pair rows out
+        "down": U * D * I * 9 // 16 + P * I * 2 + P * D * yb,
         # per-pair rows in, bf16 out
-        "combine": P * D * 4 + T * D * 2 + T * k * 8,
+        "combine": P * D * yb + T * D * 2 + T * k * 8,
     }
 
 
@@ -318,9 +326,10 @@ def measure_prefill(T, steps, warmup, layers=2):
 def run_ours_single(args):
     import torch
     from expert_sniper_b200 import MoEBlock, PRESETS, prepare_packed
+    from expert_sniper_b200.block import ffn_kernels
     from expert_sniper_b200.quant import cache_bias_vector, synthetic_inputs, synthetic_layer
 
-    cfg = PRESETS["qwen3-30b-a3b"]
+    cfg = PRESETS["qwen3-30b-a3b"].with_(kernel_path=args.kernel_path)
     dev = torch.device("cuda:0")
     torch.cuda.set_device(dev)
     T, L = args.tokens, args.layers
@@ -426,9 +435,11 @@ def run_ours_single(args):
         mean_bytes = sum(block_bytes(cfg, Tc, U[s % L]) for s in range(W, W + K)) / K
         prof = profile_kernels(xs, lgs, outs, min(K, 4 * L))
         kmean = {k: statistics.mean(v for _, v in prof[k]) for k in KERNELS}
-        kb = {k: statistics.mean(kernel_bytes(cfg, Tc, U[l])[k] for l, _ in prof[k]) for k in KERNELS}
+        path_c = ffn_kernels(cfg, Tc)
+        kb = {k: statistics.mean(kernel_bytes(cfg, Tc, U[l], path_c)[k] for l, _ in prof[k])
+              for k in KERNELS}
         results[Tc] = dict(ms=ms, bytes=mean_bytes, U=statistics.mean(U), U_layers=U, kmean=kmean,
-                           kb=kb, clocks=clk, xs=xs, lgs=lgs, outs=outs)
+                           kb=kb, clocks=clk, xs=xs, lgs=lgs, outs=outs, path=path_c)
 
     # e2e through the public API with host buffers
     r = results[T]
@@ -470,7 +481,7 @@ def run_ours_single(args):
     tp = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tp):
         with open(tp) as f:
-            rec = json.load(f).get(f"{cfg.name}:T{T}:{dom}")
+            rec = json.load(f).get(f"{cfg.name}:T{T}:{r['path']}:{dom}")
         if rec:
             traffic = rec["dram_bytes"] * r["kb"][dom] / rec["algorithmic_bytes"]
     line = {
@@ -499,14 +510,18 @@ def run_ours_single(args):
         "e2e": {"value": T / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": T * cfg.hidden * 2 + T * cfg.num_experts * 2,
                 "d2h_bytes_per_step": T * cfg.hidden * 2, "ms_per_step": e2e_ms},
-        "gpu_launches": 4 * args.steps,  # front, gate/up, down, combine per step
+        # per step: decode kernels front, gate/up, down, combine; tensor-core
+        # kernels front, scatter, gate/up, down, combine
+        "gpu_launches": (4 if r["path"] == "decode" else 5) * args.steps,
+        "kernel_path": r["path"],
         "clocks": r["clocks"],
         "cpu_baseline": cpu,
         "sweep": [{"tokens": Tc, "ms_per_step": results[Tc]["ms"],
                    "value": Tc / (results[Tc]["ms"] * 1e-3),
                    "gbs": results[Tc]["bytes"] / (results[Tc]["ms"] * 1e-3) / 1e9,
                    "frac": results[Tc]["bytes"] / (results[Tc]["ms"] * 1e-3) / 1e9 / peak,
-                   "kernel_ms": results[Tc]["kmean"]} for Tc in sweep],
+                   "kernel_ms": results[Tc]["kmean"], "kernel_path": results[Tc]["path"]}
+                  for Tc in sweep],
         "setup_s": setup_s,
     }
     if not args.no_prefill:

@@ -88,14 +88,14 @@ def ffn_kernels(cfg: MoEConfig, T: int) -> str:
     """The expert-FFN kernels a call with T tokens runs ("decode", "tensor"
     or "tensor-small"): the rule of es_moe_cfg.kernel_path in
     include/es_moe.h (automatic: by the average pairs per routed expert
-    p = T k / E, decode below 8, 32-token tiles up to 32, 128-token tiles
+    p = T k / E, decode below 4, 32-token tiles up to 48, 128-token tiles
     above, tensor-core kernels only from T = 64)."""
     if cfg.kernel_path != "auto":
         return cfg.kernel_path
     pk = T * cfg.top_k
-    if T >= 64 and pk > 32 * cfg.num_experts:
+    if T >= 64 and pk > 48 * cfg.num_experts:
         return "tensor"
-    if T >= 64 and pk >= 8 * cfg.num_experts:
+    if T >= 64 and pk >= 4 * cfg.num_experts:
         return "tensor-small"
     return "tensor-small" if cfg.x_dtype == "f16" else "decode"
 

@@ -37,7 +37,7 @@ es_status check_cfg(const es_moe_cfg* c) {
 // 1 = tensor-core GEMMs with 128-token tiles (A in shared memory), 2 = tensor-
 // core GEMMs with 32-token tiles (A in tensor memory). Automatic, by the
 // average (token, expert) pairs per routed expert p = T k / E (and T >= 64):
-// decode below p = 8, 32-token tiles up to p = 32, 128-token tiles above --
+// decode below p = 4, 32-token tiles up to p = 48, 128-token tiles above --
 // the crossovers measured on a B200 for the Qwen3-30B and Qwen3-Next layers.
 enum { kFfnDecode = 0, kFfnTensorLarge = 1, kFfnTensorSmall = 2 };
 int ffn_variant(const es_moe_cfg* c, int T) {
@@ -45,8 +45,8 @@ int ffn_variant(const es_moe_cfg* c, int T) {
   if (c->kernel_path == 2) return kFfnTensorLarge;
   if (c->kernel_path == 1) return kFfnDecode;  // (fp16 x is rejected with path 1)
   const long long pk = (long long)T * c->top_k;
-  if (T >= 64 && pk > 32LL * c->num_experts) return kFfnTensorLarge;
-  if (T >= 64 && pk >= 8LL * c->num_experts) return kFfnTensorSmall;
+  if (T >= 64 && pk > 48LL * c->num_experts) return kFfnTensorLarge;
+  if (T >= 64 && pk >= 4LL * c->num_experts) return kFfnTensorSmall;
   // fp16 activations are read by the tensor-core kernels only
   return c->x_dtype == ES_DTYPE_F16 ? kFfnTensorSmall : kFfnDecode;
 }

@@ -404,18 +404,32 @@ constexpr int kRun = 4 * kTileBytes;  // four contiguous 576-byte tiles
 template <bool GU, int NT, bool TA>
 struct PfCfg {
   static constexpr int kProj = GU ? 2 : 1;
-  static constexpr int kTiles = 8 * kProj;  // 16-row tiles per K-block
-  static constexpr int kRawBytes = kTiles * kTileBytes;
+  // quantisation groups (64 columns each) per pipeline stage: two for the
+  // small-tile variant, whose stages are otherwise too small to cover the
+  // fixed cost of each barrier hand-off
+  static constexpr int kKG = TA ? 2 : 1;
+  static constexpr int kTiles = 8 * kProj;  // 16-row tiles per group
+  static constexpr int kRawBytes = kKG * kTiles * kTileBytes;
   static constexpr int kABytes = kM * 128;  // one projection (shared-memory A)
   static constexpr int kAStage = TA ? 0 : kProj * kABytes;
-  static constexpr int kBStage = NT * 128;
+  static constexpr int kBStage = kKG * NT * 128;  // one 128-byte-swizzled [NT x 64] block per group
   static constexpr int kRawStages = TA ? 8 : (GU ? 3 : 6);
-  static constexpr int kOpStages = TA ? (GU ? 6 : 8) : (GU ? 4 : 6);  // A and B share barriers
-  static constexpr int kNumDqWarps = TA ? 4 : 8;                 // warps per K-block
-  static constexpr int kDqGroups = kDqWarps / kNumDqWarps;       // take K-blocks in turn
+  static constexpr int kOpStages = TA ? (GU ? 3 : 7) : (GU ? 4 : 6);  // A and B share barriers
+  // warps per stage: small-tile variant, one per (TMEM lane quarter, group
+  // of the stage); otherwise one per 16-row block
+  static constexpr int kNumDqWarps = TA ? 4 * kKG : 8;
+  // groups of kNumDqWarps taking stages in turn. A group waits on a slot's
+  // empty barrier for the stage kOpStages before its own; with more groups
+  // than slots it could run two phases ahead of that barrier, where parity
+  // waits cannot tell the phases apart -- so at most kOpStages groups work
+  // (the gate/up small-tile kernel: 3 slots, 3 groups, the last 4 warps idle)
+  static constexpr int kDqGroups =
+      kDqWarps / kNumDqWarps < kOpStages ? kDqWarps / kNumDqWarps : kOpStages;
+  static_assert(!TA || kNumDqWarps * kDqGroups <= kDqWarps, "dequant warps");
+  static_assert(kDqGroups <= kOpStages && kDqGroups >= 1, "dequant groups vs operand slots");
   static constexpr size_t kRawRing = (size_t)kRawStages * kRawBytes;
   static constexpr int kAccCols = kProj * NT;
-  static constexpr int kACols = TA ? kProj * (kGroup / 2) : 0;   // TMEM A columns per slot
+  static constexpr int kACols = TA ? kKG * kProj * (kGroup / 2) : 0;  // TMEM A columns per slot
   static constexpr int kTmemCols = TA ? 512 : 2 * kAccCols;      // power of two >= 32
   static_assert(2 * kAccCols + kOpStages * kACols <= kTmemCols, "tensor memory budget");
   static_assert(NT % 32 == 0 && NT <= 128, "token tile");
@@ -434,10 +448,11 @@ ES_DEV void tma_tile2d(void* dst, const CUtensorMap* tm, int col, int row, uint6
       : "memory");
 }
 
-// One K-block of a unit's code tiles (its 16-row tiles for one quantisation
-// group: runs of four contiguous 576-byte tiles, GD (or KG) runs apart) with
-// one 5-D TMA load: 8-byte elements, dims {144, 2, group, run, expert}, box
-// {144, 2, 1, runs, 1}, x coordinate 0; lands as the runs back to back.
+// One stage of a unit's code tiles (its 16-row tiles for kKG consecutive
+// quantisation groups: runs of four contiguous 576-byte tiles) with one 5-D
+// TMA load: 8-byte elements, dims {144, 2, group, run, expert}, box
+// {144, 2, kKG, runs, 1}, x coordinate 0; lands run by run, each run's
+// groups back to back.
 ES_DEV void tma_codes5d(void* dst, const CUtensorMap* tm, int group, int run0, int expert,
                         uint64_t* bar, uint64_t pol) {
   asm volatile(
@@ -602,7 +617,7 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
 
   const uint32_t tmem = s_tmem;
   const int RB = (GU ? a.I : a.D) / kM;
-  const int KB = (GU ? a.D : a.I) / kGroup;
+  const int KB = (GU ? a.D : a.I) / (kGroup * C::kKG);  // stages per unit
   const int units = s_ts[n_act] * RB;
 
   if (warp == kWarpLoad) {
@@ -626,7 +641,8 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
           mbar_arrive_expect_tx(&raw_full[s], C::kRawBytes);
           uint8_t* dst = raw + (size_t)s * C::kRawBytes;
           if (TA) {
-            tma_codes5d(dst, &a.tm_a, kb, (C::kRawBytes / kRun) * un.rb, un.e, &raw_full[s], pol);
+            tma_codes5d(dst, &a.tm_a, kb * C::kKG, (C::kRawBytes / (kRun * C::kKG)) * un.rb, un.e,
+                        &raw_full[s], pol);
           } else {
 #pragma unroll
             for (int p = 0; p < C::kRawBytes / kRun; ++p) {
@@ -668,16 +684,21 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
         tc_fence_after();
         const uint64_t bdesc = sw128_desc(sb + (size_t)so * C::kBStage);
         if (TA) {
-          // A slot so: columns [2 kAccCols + so kACols, + kACols), 32 per
-          // projection, 8 per K = 16 step
+          // A slot so: columns [2 kAccCols + so kACols, + kACols): per
+          // projection kKG groups of 32 columns, 8 per K = 16 step; B: one
+          // [NT x 64] swizzled block per group (NT * 128 bytes = NT * 8
+          // descriptor units apart)
           const uint32_t a0 = tmem + 2 * C::kAccCols + so * C::kACols;
           if (elect_one()) {
 #pragma unroll
             for (int pj = 0; pj < C::kProj; ++pj)
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                umma_f16_ts(d0 + pj * kNT, a0 + pj * (kGroup / 2) + 8 * kk, bdesc + 2 * kk, idesc,
-                            (kb > 0 || kk > 0) ? 1u : 0u);
+              for (int g2 = 0; g2 < C::kKG; ++g2)
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                  umma_f16_ts(d0 + pj * kNT, a0 + (pj * C::kKG + g2) * (kGroup / 2) + 8 * kk,
+                              bdesc + (uint64_t)g2 * (kNT * 8) + 2 * kk, idesc,
+                              (kb > 0 || g2 > 0 || kk > 0) ? 1u : 0u);
             umma_commit(&op_empty[so]);
           }
         } else {
@@ -735,17 +756,21 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
           if (aborted()) { ok = false; break; }
           uint8_t* dst = sb + (size_t)s * C::kBStage;
 #pragma unroll
-          for (int i = 0; i < kNT / 8; ++i) {
-            const int j = r0 + 8 * i;
-            if (rows[i]) cp_async16(dst + j * 128 + ((ch ^ (j & 7)) << 4), rows[i] + kb * kGroup);
-          }
+          for (int g2 = 0; g2 < C::kKG; ++g2)
+#pragma unroll
+            for (int i = 0; i < kNT / 8; ++i) {
+              const int j = r0 + 8 * i;
+              if (rows[i])
+                cp_async16(dst + g2 * (kNT * 128) + j * 128 + ((ch ^ (j & 7)) << 4),
+                           rows[i] + (kb * C::kKG + g2) * kGroup);
+            }
           cp_async_arrive(&op_full[s]);
           mbar_arrive(&op_full[s]);
         }
       }
       cp_async_wait_all();
     } else if (warp == kWarpB) {
-      // 128 consecutive pair rows of h16: one TMA tile per K-block
+      // NT consecutive pair rows of h16: one TMA tile per group
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         const Unit un = decode_unit<NT>(a, s_ts, n_act, RB, u);
         for (int kb = 0; kb < KB; ++kb, ++q) {
@@ -758,7 +783,10 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
           if (aborted()) { ok = false; break; }
           if (lane == 0) {
             mbar_arrive_expect_tx(&op_full[s], (uint32_t)C::kBStage);
-            tma_tile2d(sb + (size_t)s * C::kBStage, &a.tm_b, kb * kGroup, un.pair0, &op_full[s]);
+#pragma unroll
+            for (int g2 = 0; g2 < C::kKG; ++g2)
+              tma_tile2d(sb + (size_t)s * C::kBStage + g2 * (kNT * 128), &a.tm_b,
+                         (kb * C::kKG + g2) * kGroup, un.pair0, &op_full[s]);
           }
         }
       }
@@ -839,17 +867,21 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
     if (!ok) { if (lane == 0) set_error(a.err, 0x8u); set_abort(); }
   } else if (TA && warp >= kWarpDq0) {
     // ---------------- codes -> fp16 A in tensor memory ----------------
-    // warp (8 + 4 grp + dw): TMEM lane quarter dw (warp % 4), so thread
-    // `lane` owns weight row r = 32 dw + lane of the unit; group grp takes
-    // K-blocks q = grp mod kDqGroups
-    const int dw = (warp - kWarpDq0) % C::kNumDqWarps;
+    // warp 8 + kNumDqWarps grp + 4 sub + dw: TMEM lane quarter dw (warp % 4),
+    // so thread `lane` owns weight row r = 32 dw + lane of the unit, and it
+    // converts quantisation group `sub` of the stage; group grp of warps
+    // takes stages q = grp mod kDqGroups (warps of groups >= kDqGroups idle)
+    const int dw = (warp - kWarpDq0) & 3;
+    const int sub = ((warp - kWarpDq0) >> 2) % C::kKG;
     const int grp = (warp - kWarpDq0) / C::kNumDqWarps;
     const int b16 = 2 * dw + (lane >> 4);  // 16-row tile of the row
     const int g = lane & 7, hf = (lane >> 3) & 1;  // row g + 8 hf of that tile
+    constexpr int kRowBlocksPerRun = 4 / C::kProj;
+    const int run = b16 / kRowBlocksPerRun, in_run = (b16 % kRowBlocksPerRun) * C::kProj;
     const uint32_t a_lane = tmem + ((uint32_t)(32 * dw) << 16) + 2 * C::kAccCols;
     int q = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+    for (int u = blockIdx.x; u < units && ok && grp < C::kDqGroups; u += gridDim.x) {
       for (int kb = 0; kb < KB; ++kb, ++q) {
         if (q % C::kDqGroups != grp) continue;
         const int sr = q % C::kRawStages, s_a = q % C::kOpStages;
@@ -858,13 +890,16 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
           ok = false;
           break;
         }
-        // the row's eight code words (words 2c, 2c+1 sit in lane 4g + c's
-        // 16 bytes, row g + 8 in the upper half) and its (scale, bias)
+        // group `sub` of the stage: the row's eight code words (words 2c,
+        // 2c+1 sit in lane 4g + c's 16 bytes, row g + 8 in the upper half)
+        // and its (scale, bias); the stage holds, per run of four tiles, the
+        // kKG groups' runs back to back
+        const uint8_t* slot = raw + (size_t)sr * C::kRawBytes + (size_t)(run * C::kKG + sub) * kRun;
         uint2 wv[C::kProj][4];
         uint32_t sbw[C::kProj];
 #pragma unroll
         for (int pj = 0; pj < C::kProj; ++pj) {
-          const uint8_t* tile = raw + (size_t)sr * C::kRawBytes + (b16 * C::kProj + pj) * kTileBytes;
+          const uint8_t* tile = slot + (in_run + pj) * kTileBytes;
 #pragma unroll
           for (int c = 0; c < 4; ++c) wv[pj][c] = ld_shared8(tile + (4 * g + c) * 16 + hf * 8);
           sbw[pj] = *reinterpret_cast<const uint32_t*>(tile + kTileCodeBytes + 8 * g + 4 * hf);
@@ -876,7 +911,7 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
           ok = false;
           break;
         }
-        if (aborted()) { ok = false; break; }
+        if (__shfl_sync(0xffffffffu, aborted() ? 1 : 0, 0)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int pj = 0; pj < C::kProj; ++pj) {
@@ -890,7 +925,7 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
             r[8 * c + 0] = o0.x; r[8 * c + 1] = o0.y; r[8 * c + 2] = o0.z; r[8 * c + 3] = o0.w;
             r[8 * c + 4] = o1.x; r[8 * c + 5] = o1.y; r[8 * c + 6] = o1.z; r[8 * c + 7] = o1.w;
           }
-          tmem_st32(a_lane + s_a * C::kACols + pj * (kGroup / 2), r);
+          tmem_st32(a_lane + s_a * C::kACols + (pj * C::kKG + sub) * (kGroup / 2), r);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -994,8 +1029,9 @@ cudaError_t encode_rows_f16(CUtensorMap* m, const void* base, int cols, long lon
 
 // 5-D map of one projection region's code tiles, 8-byte elements:
 // {144, 2} = one 2304-byte run, then group (stride 2304 B), run (stride
-// groups x 2304 B), expert (stride expert_bytes); box {144, 2, 1, runs, 1}
-cudaError_t encode_codes_map(CUtensorMap* m, const PfArgs& a, bool gu, int runs) {
+// groups x 2304 B), expert (stride expert_bytes); box {144, 2, groups per
+// stage, runs, 1}
+cudaError_t encode_codes_map(CUtensorMap* m, const PfArgs& a, bool gu, int runs, int groups_per_box) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (!enc) return cudaErrorNotSupported;
   const int groups = (gu ? a.D : a.I) / kGroup;
@@ -1005,7 +1041,7 @@ cudaError_t encode_codes_map(CUtensorMap* m, const PfArgs& a, bool gu, int runs)
                               (cuuint64_t)a.E1};
   const cuuint64_t strides[4] = {kRun / 2, kRun, (cuuint64_t)groups * kRun,
                                  (cuuint64_t)a.expert_bytes};
-  const cuuint32_t box[5] = {kRun / 16, 2, 1, (cuuint32_t)runs, 1};
+  const cuuint32_t box[5] = {kRun / 16, 2, (cuuint32_t)groups_per_box, (cuuint32_t)runs, 1};
   const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 5, const_cast<uint8_t*>(base), dims,
                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -1027,8 +1063,9 @@ cudaError_t launch_pf_gemm(const PfArgs& a_in, long long b_rows, int max_units,
   cudaError_t e = GU ? cudaSuccess : encode_rows_f16(&a.tm_b, a.h16, a.I, b_rows, NT);
   if (e != cudaSuccess) return e;
   if (TA) {
-    static_assert(C::kRawBytes % kRun == 0, "whole runs per K-block");
-    e = encode_codes_map(&a.tm_a, a, GU, C::kRawBytes / kRun);
+    static_assert(C::kRawBytes % (kRun * C::kKG) == 0, "whole runs per stage");
+    if (((GU ? a.D : a.I) / kGroup) % C::kKG != 0) return cudaErrorInvalidValue;
+    e = encode_codes_map(&a.tm_a, a, GU, C::kRawBytes / (kRun * C::kKG), C::kKG);
     if (e != cudaSuccess) return e;
   }
   e = cudaFuncSetAttribute(pf_gemm_kernel<GU, NT, TA>,

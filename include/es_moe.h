@@ -82,8 +82,8 @@ typedef struct es_moe_cfg {
                            *   0 = automatic, by the average (token,
                            *       expert) pairs per routed expert
                            *       p = T * top_k / num_experts: with
-                           *       T >= 64, path 2 for p > 32, path 3 for
-                           *       8 <= p <= 32; the decode path otherwise
+                           *       T >= 64, path 2 for p > 48, path 3 for
+                           *       4 <= p <= 48; the decode path otherwise
                            *       (path 3 for fp16 x);
                            *   1 = decode path (register-operand GEMV on the
                            *       4-bit codes, fp32 per-pair rows);

@@ -117,19 +117,22 @@ def test_config_validation_in_python():
 
 def test_automatic_kernel_choice():
     """The automatic expert-FFN kernel rule (es_moe_cfg.kernel_path 0), by
-    average pairs per routed expert p = T k / E: decode below 8, 32-token
-    tensor tiles up to 32, 128-token tiles above; tensor kernels from T = 64;
+    average pairs per routed expert p = T k / E: decode below 4, 32-token
+    tensor tiles up to 48, 128-token tiles above; tensor kernels from T = 64;
     fp16 activations never take the decode kernels."""
     from expert_sniper_b200.block import ffn_kernels, uses_tensor_path
     q = PRESETS["qwen3-30b-a3b"]          # E = 128, k = 8
-    assert [ffn_kernels(q, T) for T in (1, 8, 64, 127, 128, 256, 512, 513, 4096)] == [
-        "decode", "decode", "decode", "decode", "tensor-small", "tensor-small", "tensor-small",
-        "tensor", "tensor"]
+    assert [ffn_kernels(q, T) for T in (1, 8, 63, 64, 128, 256, 768, 769, 4096)] == [
+        "decode", "decode", "decode", "tensor-small", "tensor-small", "tensor-small",
+        "tensor-small", "tensor", "tensor"]
     small = MoEConfig(256, 4, 2, 256, True)  # p = T / 2: the T >= 64 floor decides
     assert ffn_kernels(small, 32) == "decode" and ffn_kernels(small, 64) == "tensor-small"
-    assert ffn_kernels(small, 66) == "tensor"
+    assert ffn_kernels(small, 98) == "tensor"
+    nxt = PRESETS["qwen3-next-80b-a3b"]     # E = 512, k = 10
+    assert [ffn_kernels(nxt, T) for T in (64, 256, 2048, 4096)] == [
+        "decode", "tensor-small", "tensor-small", "tensor"]
     f16 = q.with_(x_dtype="f16")
     assert ffn_kernels(f16, 8) == "tensor-small" and ffn_kernels(f16, 4096) == "tensor"
     for path in ("decode", "tensor", "tensor-small"):
         assert ffn_kernels(q.with_(kernel_path=path), 64) == path
-    assert not uses_tensor_path(q, 64) and uses_tensor_path(q, 128)
+    assert not uses_tensor_path(q, 63) and uses_tensor_path(q, 64)
