@@ -1,0 +1,62 @@
+"""bench.py's accounting on the CPU: the algorithmic bytes per kernel for
+each expert-FFN kernel family (the roofline numerators), the traffic
+records it scales, and the peak it divides by."""
+from __future__ import annotations
+
+import importlib.util
+import json
+import os
+
+from expert_sniper_b200 import PRESETS
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _bench():
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_kernel_bytes_by_kernel_family():
+    b = _bench()
+    cfg = PRESETS["qwen3-30b-a3b"]
+    D, I, k = cfg.hidden, cfg.inter, cfg.top_k
+    T, U = 64, 120
+    P = T * k
+    dec = b.kernel_bytes(cfg, T, U, "decode")
+    ts = b.kernel_bytes(cfg, T, U, "tensor-small")
+    # weights read once per distinct expert, activations in, fp16 h out
+    assert dec["gateup"] == ts["gateup"] == U * 2 * D * I * 9 // 16 + T * D * 2 + P * I * 2
+    # per-pair rows: fp32 on the decode kernels, fp16 on the tensor-core ones
+    assert dec["down"] - ts["down"] == P * D * 2
+    assert dec["combine"] - ts["combine"] == P * D * 2
+    # prepared activations: 64-column sums (decode) vs one scale per token
+    assert dec["front"] - ts["front"] == T * (D // 64) * 4 - T * 4
+    assert b.kernel_bytes(cfg, T, U, "tensor") == ts
+    assert b.kernel_bytes(cfg, T, U) == dec
+
+
+def test_block_bytes_counts_distinct_experts():
+    b = _bench()
+    cfg = PRESETS["qwen3-30b-a3b"]
+    one = b.block_bytes(cfg, 64, 1)
+    assert b.block_bytes(cfg, 64, 2) - one == cfg.bytes_per_expert
+
+
+def test_traffic_records_name_their_kernel_family():
+    with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+        rec = json.load(f)
+    fams = {"decode", "tensor", "tensor-small"}
+    for key, v in rec.items():
+        model, t, fam, kernel = key.split(":")
+        assert model in PRESETS and t.startswith("T") and fam in fams and kernel
+        # DRAM traffic within a few percent of the algorithmic bytes: no re-reads
+        assert 1.0 <= v["dram_bytes"] / v["algorithmic_bytes"] < 1.05
+
+
+def test_measured_peak():
+    b = _bench()
+    hbm, kind = b.measured_peaks()
+    assert kind in ("measured", "fallback") and hbm > 1000
