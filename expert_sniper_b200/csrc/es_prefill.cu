@@ -1,12 +1,18 @@
-// Tensor-core path of the MoE block for large batches (prefill): the expert
-// FFN as a grouped GEMM on the 5th-generation tensor cores (tcgen05.mma,
-// accumulators in tensor memory), with the 4-bit weights dequantised to fp16
-// in shared memory on the way.
+// Tensor-core path of the MoE block: the expert FFN as a grouped GEMM on the
+// 5th-generation tensor cores (tcgen05.mma, accumulators in tensor memory),
+// with the 4-bit weights dequantised to fp16 on the way. Two variants of the
+// GEMM share this file (template parameter TA):
+//   large batches (prefill): 128-token tiles, the dequantised weights in
+//     128-byte-swizzled shared memory;
+//   small batches (from 4 pairs per routed expert): 32-token tiles, the
+//     dequantised weights written straight into tensor memory and read
+//     from there by the MMA (A operand in TMEM), two quantisation groups
+//     per pipeline stage, each stage's code tiles fetched with one 5-D TMA.
 //
 // Restates the same math as the decode kernels (engine.py:32-41 gather_qmm
 // gate/up, SwiGLU, gather_qmm down; generate.py:173-178 shared expert), for
-// batches where each expert sees many tokens, so weights are read once per
-// 128-token tile instead of once per few tokens.
+// batches where each expert sees enough tokens that one weight read feeds a
+// tensor-core tile.
 //
 // Kernels, in launch order (one stream, programmatic dependent launches):
 //   pf_front    router (generate.py:122-136) per token; per-expert slot
@@ -17,31 +23,35 @@
 //               per-token power-of-two scale, in nibble order. The last CTA
 //               scans the counts into expert offsets and the active list.
 //   pf_scatter  slot -> pair index, pair -> token.
-//   pf_gemm<1>  gate/up: per unit (expert, 128 rows of I, <=128 tokens) two
+//   pf_gemm<1>  gate/up: per unit (expert, 128 rows of I, one token tile) two
 //               accumulators [128 x N] in TMEM; epilogue SwiGLU -> fp16 h.
-//   pf_gemm<0>  down: per unit (expert, 128 rows of D, <=128 tokens) one
+//   pf_gemm<0>  down: per unit (expert, 128 rows of D, one token tile) one
 //               accumulator; epilogue -> fp16 per-pair rows (saturated
 //               and flagged beyond the fp16 range, as h is).
 //   combine     (es_combine.cu) fixed expert-id order, fp32.
 //
-// GEMM orientation: A = weights (M = 128 rows, K-major, dequantised into a
-// 128-byte-swizzled smem tile), B = activations of the unit's tokens
-// (N = tokens rounded up to 16, K-major, gathered rows), D = A * B^T in TMEM
-// (lane = weight row, column = token). Weights are the large operand and are
-// read from HBM exactly once per token tile.
+// GEMM orientation: A = weights (M = 128 rows, K-major), B = activations of
+// the unit's tokens (N = tokens rounded up to 16, K-major, gathered rows in
+// 128-byte-swizzled shared memory), D = A * B^T in TMEM (lane = weight row,
+// column = token). Weights are the large operand and are read from HBM
+// exactly once per token tile.
 //
 // Warp roles of the persistent CTA (24 warps, one CTA per SM):
-//   warp 0      bulk-copies the packed code tiles of each K-block (64 columns,
-//               one quantisation group) into a ring (raw_full / raw_empty)
+//   warp 0      copies the packed code tiles of each stage into a ring
+//               (raw_full / raw_empty): bulk copies of 2304-byte runs, or
+//               one 5-D TMA load per stage in the small-tile variant
 //   warp 1      allocates TMEM; one lane issues tcgen05.mma and commits
 //   warps 2-3   load the B rows into their ring: gate/up gathers token rows
 //               of x16 with cp.async (completion tracked on the ring's
-//               mbarrier), down copies 128 consecutive pair rows of h16 with
-//               one TMA tile load per K-block
+//               mbarrier), down copies consecutive pair rows of h16 with
+//               one TMA tile load per quantisation group
 //   warps 4-7   epilogue: tcgen05.ld from TMEM, math, global stores
-//   warps 8-23  dequantise codes -> fp16 A tiles in their ring: two groups
-//               of eight warps take alternate K-blocks, one 16-row block per
-//               warp
+//   warps 8-23  dequantise codes -> fp16 A: large tiles, two groups of
+//               eight warps take alternate stages, one 16-row block per warp
+//               (st.shared in the swizzled layout); small tiles, two groups
+//               of eight warps, one per (TMEM lane quarter, quantisation
+//               group of the stage), one weight row per thread
+//               (tcgen05.st)
 // Every wait is bounded (ES_DEVERR_TIMEOUT); on a timeout each role stops,
 // copies in flight are waited for, and TMEM is freed before returning.
 #include <cudaTypedefs.h>
