@@ -110,7 +110,7 @@ struct PfScatterArgs {
 // Grouped GEMM over (active expert, 128-row block, token tile) units.
 struct alignas(64) PfArgs {
   CUtensorMap tm_b;         // B rows: x16 (gate/up) or h16 (down); set by the launcher
-  CUtensorMap tm_a;         // packed code tiles (small-tile variant); set by the launcher
+  CUtensorMap tm_a;         // packed code tiles, one 5-D box per stage; set by the launcher
   const uint8_t* packed;
   size_t expert_bytes;
   int D, I;

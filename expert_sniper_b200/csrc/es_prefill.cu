@@ -634,12 +634,10 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
     // ---------------- packed code tiles -> raw ring ----------------
     if (lane == 0) {
       const uint64_t pol = l2_evict_first_policy();
-      const int GD = a.D / kGroup;
       int q = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         const Unit un = decode_unit<NT>(a, s_ts, n_act, RB, u);
-        const uint8_t* eb = a.packed + (size_t)un.e * a.expert_bytes;
         for (int kb = 0; kb < KB; ++kb, ++q) {
           const int s = q % C::kRawStages;
           if (!mbar_wait_bounded(&raw_empty[s], ((q / C::kRawStages) & 1) ^ 1)) {
@@ -649,18 +647,8 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
           }
           if (aborted()) { ok = false; break; }
           mbar_arrive_expect_tx(&raw_full[s], C::kRawBytes);
-          uint8_t* dst = raw + (size_t)s * C::kRawBytes;
-          if (TA) {
-            tma_codes5d(dst, &a.tm_a, kb * C::kKG, (C::kRawBytes / (kRun * C::kKG)) * un.rb, un.e,
-                        &raw_full[s], pol);
-          } else {
-#pragma unroll
-            for (int p = 0; p < C::kRawBytes / kRun; ++p) {
-              const size_t off = GU ? gateup_tile_off(GD, 2 * (un.rb * 4 + p), kb, 0)
-                                    : down_tile_off(a.D, a.I, 4 * (un.rb * 2 + p), kb);
-              bulk_copy_g2s(dst + p * kRun, eb + off, kRun, &raw_full[s], pol);
-            }
-          }
+          tma_codes5d(raw + (size_t)s * C::kRawBytes, &a.tm_a, kb * C::kKG,
+                      (C::kRawBytes / (kRun * C::kKG)) * un.rb, un.e, &raw_full[s], pol);
         }
       }
       if (!ok) { set_error(a.err, 0x8u); set_abort(); }
@@ -1072,12 +1060,10 @@ cudaError_t launch_pf_gemm(const PfArgs& a_in, long long b_rows, int max_units,
   // gathers token rows with cp.async and needs no tensor map
   cudaError_t e = GU ? cudaSuccess : encode_rows_f16(&a.tm_b, a.h16, a.I, b_rows, NT);
   if (e != cudaSuccess) return e;
-  if (TA) {
-    static_assert(C::kRawBytes % (kRun * C::kKG) == 0, "whole runs per stage");
-    if (((GU ? a.D : a.I) / kGroup) % C::kKG != 0) return cudaErrorInvalidValue;
-    e = encode_codes_map(&a.tm_a, a, GU, C::kRawBytes / (kRun * C::kKG), C::kKG);
-    if (e != cudaSuccess) return e;
-  }
+  static_assert(C::kRawBytes % (kRun * C::kKG) == 0, "whole runs per stage");
+  if (((GU ? a.D : a.I) / kGroup) % C::kKG != 0) return cudaErrorInvalidValue;
+  e = encode_codes_map(&a.tm_a, a, GU, C::kRawBytes / (kRun * C::kKG), C::kKG);
+  if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(pf_gemm_kernel<GU, NT, TA>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
   if (e != cudaSuccess) return e;
