@@ -414,17 +414,18 @@ constexpr int kRun = 4 * kTileBytes;  // four contiguous 576-byte tiles
 template <bool GU, int NT, bool TA>
 struct PfCfg {
   static constexpr int kProj = GU ? 2 : 1;
-  // quantisation groups (64 columns each) per pipeline stage: two for the
-  // small-tile variant, whose stages are otherwise too small to cover the
-  // fixed cost of each barrier hand-off
-  static constexpr int kKG = TA ? 2 : 1;
+  // quantisation groups (64 columns each) per pipeline stage: the small-tile
+  // variant's stages are otherwise too small to cover the fixed cost of each
+  // barrier hand-off -- 2 for gate/up (two projections per group already),
+  // 4 for down, both 18 KB of codes per stage
+  static constexpr int kKG = TA ? (GU ? 2 : 4) : 1;
   static constexpr int kTiles = 8 * kProj;  // 16-row tiles per group
   static constexpr int kRawBytes = kKG * kTiles * kTileBytes;
   static constexpr int kABytes = kM * 128;  // one projection (shared-memory A)
   static constexpr int kAStage = TA ? 0 : kProj * kABytes;
   static constexpr int kBStage = kKG * NT * 128;  // one 128-byte-swizzled [NT x 64] block per group
   static constexpr int kRawStages = TA ? 8 : (GU ? 3 : 6);
-  static constexpr int kOpStages = TA ? (GU ? 3 : 7) : (GU ? 4 : 6);  // A and B share barriers
+  static constexpr int kOpStages = TA ? 3 : (GU ? 4 : 6);  // A and B share barriers
   // warps per stage: small-tile variant, one per (TMEM lane quarter, group
   // of the stage); otherwise one per 16-row block
   static constexpr int kNumDqWarps = TA ? 4 * kKG : 8;
