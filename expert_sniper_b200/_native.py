@@ -66,6 +66,7 @@ _SIGNATURES = {
     "es_dec_add_rmsnorm": (ctypes.c_int, [_P, _P, _P, _P, _I32, _I32, ctypes.c_float, _P]),
     "es_dec_qk_norm_rope_kv": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32,
                                               _I32, _I32, _I32, ctypes.c_float, _P]),
+    "es_dec_gemv": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I32, _P]),
 }
 
 _lib = None

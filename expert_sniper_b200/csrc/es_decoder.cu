@@ -1,9 +1,9 @@
 // Caller-side helpers for the decoder around the MoE block (the per-layer
 // loop of src/mlx_expert_sniper/generate.py:114-122): fused residual add +
-// RMS norm, and the per-head q/k RMS norm + rotary embedding + KV-cache write
-// of Qwen3 attention. Plain elementwise/reduction kernels in fp32 arithmetic
-// on bf16 tensors; no counterpart in the reference beyond the MLX ops they
-// fuse.
+// RMS norm, the per-head q/k RMS norm + rotary embedding + KV-cache write of
+// Qwen3 attention, and a weight-streaming GEMV for the projections at batch
+// 1-4. Plain kernels in fp32 arithmetic on bf16 tensors; no counterpart in
+// the reference beyond the MLX ops they replace.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -96,9 +96,118 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* qkv, const uint16_t* qn, 
   }
 }
 
+// y[b][n] = sum_k W[n][k] x[b][k] for a few vectors (B <= kGemvMaxB): the
+// weight-streaming shape of a decode step at batch 1-4. One warp per
+// kGemvRows output rows; each lane reads 16-byte runs of the weight rows
+// (coalesced: a warp covers 256 consecutive columns of a row per load),
+// kGemvUnroll loads per row in flight before their use; the x vectors sit in
+// shared memory; fp32 accumulation, one warp reduction per (row, vector).
+constexpr int kGemvMaxB = 4;
+constexpr int kGemvRows = 2;
+constexpr int kGemvWarps = 8;
+constexpr int kGemvUnroll = 4;
+
+template <int B>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const uint16_t* __restrict__ w,
+                                                               const uint16_t* __restrict__ x,
+                                                               uint16_t* __restrict__ y, int N,
+                                                               int K) {
+  extern __shared__ uint4 s_x4[];  // [B][K / 8]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int k8 = K / 8;
+  for (int i = threadIdx.x; i < B * k8; i += blockDim.x)
+    s_x4[i] = reinterpret_cast<const uint4*>(x)[i];
+  __syncthreads();
+  const int n0 = (blockIdx.x * kGemvWarps + warp) * kGemvRows;
+  if (n0 >= N) return;
+  float acc[kGemvRows][B];
+#pragma unroll
+  for (int r = 0; r < kGemvRows; ++r)
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[r][b] = 0.f;
+  for (int c0 = lane; c0 < k8; c0 += 32 * kGemvUnroll) {
+    uint4 wv[kGemvUnroll][kGemvRows];
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; ++u)
+#pragma unroll
+      for (int r = 0; r < kGemvRows; ++r) {
+        const int c = c0 + 32 * u;
+        wv[u][r] = (c < k8 && n0 + r < N)
+                       ? __ldcs(reinterpret_cast<const uint4*>(w + (size_t)(n0 + r) * K) + c)
+                       : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; ++u) {
+      const int c = c0 + 32 * u;
+      if (c >= k8) break;
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const uint4 xv = s_x4[b * k8 + c];
+        const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int r = 0; r < kGemvRows; ++r) {
+          const uint32_t ws[4] = {wv[u][r].x, wv[u][r].y, wv[u][r].z, wv[u][r].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            acc[r][b] = fmaf(__uint_as_float(ws[q] << 16), __uint_as_float(xs[q] << 16), acc[r][b]);
+            acc[r][b] = fmaf(__uint_as_float(ws[q] & 0xffff0000u),
+                             __uint_as_float(xs[q] & 0xffff0000u), acc[r][b]);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kGemvRows; ++r)
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      float v = acc[r][b];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0 && n0 + r < N) y[(size_t)b * N + n0 + r] = to_bf(v);
+    }
+}
+
+template <int B>
+cudaError_t launch_gemv(const uint16_t* w, const uint16_t* x, uint16_t* y, int N, int K,
+                        cudaStream_t st) {
+  const size_t smem = (size_t)B * K * 2;
+  if (smem > 48 * 1024) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(gemv_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  const int rows_per_block = kGemvWarps * kGemvRows;
+  gemv_kernel<B><<<(N + rows_per_block - 1) / rows_per_block, kGemvWarps * 32, smem, st>>>(w, x, y,
+                                                                                           N, K);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 extern "C" {
+
+es_status es_dec_gemv(const void* weight, const void* x, void* y, int32_t batch, int32_t n,
+                      int32_t k, es_stream_t stream) {
+  if (!weight || !x || !y || batch < 0 || batch > kGemvMaxB || n <= 0 || k <= 0 || k % 8 ||
+      (size_t)batch * k * 2 > 200 * 1024)
+    return ES_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(weight) % 16 || reinterpret_cast<uintptr_t>(x) % 16)
+    return ES_ERR_INVALID_ARG;
+  if (batch == 0) return ES_OK;
+  const auto* w = static_cast<const uint16_t*>(weight);
+  const auto* xv = static_cast<const uint16_t*>(x);
+  auto* yv = static_cast<uint16_t*>(y);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
+  switch (batch) {
+    case 1: e = launch_gemv<1>(w, xv, yv, n, k, st); break;
+    case 2: e = launch_gemv<2>(w, xv, yv, n, k, st); break;
+    case 3: e = launch_gemv<3>(w, xv, yv, n, k, st); break;
+    default: e = launch_gemv<4>(w, xv, yv, n, k, st); break;
+  }
+  return e == cudaSuccess ? ES_OK : ES_ERR_CUDA;
+}
 
 es_status es_dec_add_rmsnorm(void* h, const void* delta, const void* weight, void* out,
                              int32_t rows, int32_t cols, float eps, es_stream_t stream) {

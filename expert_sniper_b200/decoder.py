@@ -21,9 +21,11 @@ replays step after step.
 
 Two forms of the code around the block, same arithmetic (fp32 math on bf16
 tensors, bf16 rounding at the same points):
-  fused=True   one q|k|v projection GEMM; the residual add + RMS norm and
+  fused=True   one q|k|v projection; the residual add + RMS norm and
                the q/k norm + rotary + cache write are single kernels of
                libes_moe.so (es_dec_add_rmsnorm, es_dec_qk_norm_rope_kv);
+               at batch <= 4 the q|k|v, output and router projections are
+               weight-streaming GEMVs (es_dec_gemv), cuBLAS above;
   fused=False  the same steps as separate torch ops (the restatement the
                fused kernels are checked against).
 Attention itself is torch's scaled_dot_product_attention in both.
@@ -102,6 +104,24 @@ def add_rmsnorm_(h: torch.Tensor, delta, w: torch.Tensor, out: torch.Tensor,
     _native.check("es_dec_add_rmsnorm", _native.lib().es_dec_add_rmsnorm(
         h.data_ptr(), 0 if delta is None else delta.data_ptr(), w.data_ptr(), out.data_ptr(),
         rows, cols, ctypes.c_float(eps), _stream(h)))
+    return out
+
+
+GEMV_MAX_BATCH = 4
+
+
+def gemv(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out = x @ w.T for x [B, K] (B <= 4), w [N, K], out [B, N], all bf16:
+    one es_dec_gemv launch (weight-streaming, fp32 accumulation)."""
+    B, K = x.shape
+    N = w.shape[0]
+    for t in (x, w, out):
+        if not (t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous()):
+            raise ValueError("gemv takes contiguous bf16 CUDA tensors")
+    if w.shape[1] != K or out.shape != (B, N) or B > GEMV_MAX_BATCH:
+        raise ValueError("gemv: shape mismatch or batch above 4")
+    _native.check("es_dec_gemv", _native.lib().es_dec_gemv(
+        w.data_ptr(), x.data_ptr(), out.data_ptr(), B, N, K, _stream(x)))
     return out
 
 
@@ -185,6 +205,12 @@ class Decoder:
         self.h = torch.empty(batch, D, dtype=torch.bfloat16, device=self.device)
         self.n = torch.empty(batch, D, dtype=torch.bfloat16, device=self.device)
         self.q = torch.empty(batch, H, hd, dtype=torch.bfloat16, device=self.device)
+        # projection outputs of the fused step (weight-streaming GEMVs at batch <= 4)
+        self.qkv_out = torch.empty(batch, (H + 2 * KV) * hd, dtype=torch.bfloat16,
+                                   device=self.device)
+        self.attn_out = torch.empty(batch, D, dtype=torch.bfloat16, device=self.device)
+        self.router_out = torch.empty(batch, mcfg.num_experts, dtype=torch.bfloat16,
+                                      device=self.device)
         self.cache_bias = [None] * dcfg.layers   # per-layer [E] routing bias, optional
         self.graph = None
 
@@ -230,19 +256,29 @@ class Decoder:
         self.logits.copy_(rms_norm(h, self.final_norm, c.eps) @ self.lm_head.t())
         self.pos.add_(1)
 
+    def _proj(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        # batch <= 4: weight-streaming GEMV; larger batches: cuBLAS
+        if self.batch <= GEMV_MAX_BATCH:
+            return gemv(x, w, out)
+        return torch.matmul(x, w.t(), out=out)
+
     def _step_fused(self):
         c = self.dcfg
         h, n = self.h, self.n
+        B, H, hd = self.batch, c.heads, c.head_dim
         torch.index_select(self.embed, 0, self.tokens, out=h)
         mask = self._mask()
         delta = None
         for i, L in enumerate(self.layers):
             add_rmsnorm_(h, delta, L["in_norm"], n, c.eps)
-            qkv_proj = n @ L["qkv"].t()
+            qkv_proj = self._proj(n, L["qkv"], self.qkv_out)
             qk_norm_rope_kv(qkv_proj, L["q_norm"], L["k_norm"], self.cos, self.sin, self.pos,
                             self.q, L["k_cache"], L["v_cache"], c.eps)
-            add_rmsnorm_(h, self._sdpa(L, self.q, mask), L["post_norm"], n, c.eps)
-            logits = n @ L["router"].t()
+            o = F.scaled_dot_product_attention(self.q.unsqueeze(2), L["k_cache"], L["v_cache"],
+                                               attn_mask=mask, scale=1.0 / math.sqrt(hd),
+                                               enable_gqa=True).reshape(B, H * hd)
+            add_rmsnorm_(h, self._proj(o, L["o"], self.attn_out), L["post_norm"], n, c.eps)
+            logits = self._proj(n, L["router"], self.router_out)
             delta = L["moe"].forward(n, logits, self.cache_bias[i])
         add_rmsnorm_(h, delta, self.final_norm, n, c.eps)
         torch.matmul(n, self.lm_head.t(), out=self.logits)

@@ -303,6 +303,13 @@ ES_API es_status es_dec_qk_norm_rope_kv(const void* qkv, const void* q_norm,
                                         int32_t head_dim, int32_t max_ctx, float eps,
                                         es_stream_t stream);
 
+/* y[b][n] = sum_k weight[n][k] * x[b][k] for b < batch (1..4), bf16 in and
+ * out, fp32 accumulation: the projections of a decode step at small batch
+ * (x @ W^T with W [n][k] row-major). k % 8 == 0, 16-byte aligned weight and
+ * x, batch * k * 2 <= 200 KB. */
+ES_API es_status es_dec_gemv(const void* weight, const void* x, void* y, int32_t batch,
+                             int32_t n, int32_t k, es_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -102,6 +102,11 @@ def test_null_and_size_checks_return_status(lib):
     assert lib.es_dec_qk_norm_rope_kv(*args, 2, 4, 2, 64, 0, 1e-6, None) == 1
     assert lib.es_dec_qk_norm_rope_kv(*([None] + args[1:]), 2, 4, 2, 64, 8, 1e-6, None) == 1
     assert lib.es_dec_qk_norm_rope_kv(*args, 0, 4, 2, 64, 8, 1e-6, None) == 0
+    assert lib.es_dec_gemv(None, 16, 16, 1, 8, 8, None) == 1
+    assert lib.es_dec_gemv(16, 16, 16, 5, 8, 8, None) == 1     # batch above 4
+    assert lib.es_dec_gemv(16, 16, 16, 1, 8, 12, None) == 1    # k not a multiple of 8
+    assert lib.es_dec_gemv(16, 24, 16, 1, 8, 8, None) == 1     # x not 16-byte aligned
+    assert lib.es_dec_gemv(16, 16, 16, 0, 8, 8, None) == 0
 
 
 def test_config_validation_in_python():

@@ -103,8 +103,11 @@ def test_graph_replay_equals_eager(cuda):
 
 def test_fused_step_matches_unfused(cuda):
     """The fused kernels (add + RMS norm, q/k norm + rotary + cache write,
-    one q|k|v GEMM) round at the same points as the torch ops they replace:
-    logits and the written cache rows agree to a few bf16 ulps."""
+    one q|k|v projection, and at batch <= 4 weight-streaming GEMVs for the
+    projections) round at the same points as the torch ops they replace;
+    the GEMVs sum in another fp32 order than cuBLAS, which can move a bf16
+    rounding by one step. Logits agree within 1e-2 x RMS plus one bf16 ulp
+    of the largest logit; the written cache rows within 2e-2 x RMS."""
     B, ctx = 3, 20
     a = Decoder(SMALL, B, ctx, max_steps=4, seed=5, fused=True)
     b = Decoder(SMALL, B, ctx, max_steps=4, seed=5, fused=False)
@@ -113,7 +116,8 @@ def test_fused_step_matches_unfused(cuda):
         la = a.step(toks).float().clone()
         lb = b.step(toks).float().clone()
         rms = float(lb.pow(2).mean().sqrt())
-        assert float((la - lb).abs().max()) <= 1e-2 * rms
+        ulp = 2.0 ** -7 * float(lb.abs().max())
+        assert float((la - lb).abs().max()) <= 1e-2 * rms + ulp
         toks = lb.argmax(-1)
     for La, Lb in zip(a.layers, b.layers):
         for name in ("k_cache", "v_cache"):

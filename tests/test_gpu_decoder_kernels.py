@@ -1,5 +1,5 @@
-"""The decoder's fused helper kernels (es_dec_add_rmsnorm,
-es_dec_qk_norm_rope_kv) against the torch ops they replace: bf16 results
+"""The decoder's helper kernels (es_dec_add_rmsnorm, es_dec_qk_norm_rope_kv,
+es_dec_gemv) against the torch ops they replace: bf16 results
 within one bf16 ulp (the fp32 sums are reduced in another order, which can
 move a rounding by one step), the residual update and the v copy bit-exact,
 cache rows other than the written position untouched."""
@@ -8,7 +8,8 @@ from __future__ import annotations
 import pytest
 import torch
 
-from expert_sniper_b200.decoder import add_rmsnorm_, apply_rope, qk_norm_rope_kv, rms_norm, rope_tables
+from expert_sniper_b200.decoder import (add_rmsnorm_, apply_rope, gemv, qk_norm_rope_kv, rms_norm,
+                                        rope_tables)
 
 pytestmark = pytest.mark.gpu
 
@@ -72,3 +73,19 @@ def test_position_outside_cache_writes_nothing(cuda):
     qk_norm_rope_kv(qkv, ones, ones, cos, sin, p, q, kc, vc, 1e-6)
     torch.cuda.synchronize()
     assert not kc.any() and not vc.any() and bool((q == 3.0).all())
+
+
+@pytest.mark.parametrize("B", [1, 2, 3, 4])
+@pytest.mark.parametrize("N,K", [(5120, 2048), (2048, 4096), (128, 2048), (37, 264)])
+def test_gemv(cuda, B, N, K):
+    """x @ W^T against an fp32 product of the same bf16 values: the kernel
+    accumulates in fp32 and rounds once to bf16, so the error is within one
+    bf16 ulp of each output plus summation-order noise."""
+    g = torch.Generator(device=cuda).manual_seed(B * N + K)
+    w = (torch.randn(N, K, generator=g, device=cuda) * 0.02).to(torch.bfloat16)
+    x = torch.randn(B, K, generator=g, device=cuda).to(torch.bfloat16)
+    out = torch.empty(B, N, dtype=torch.bfloat16, device=cuda)
+    gemv(x, w, out)
+    ref = x.float() @ w.float().t()
+    rms = float(ref.pow(2).mean().sqrt())
+    assert bool(((out.float() - ref).abs() <= ref.abs() * ULP + 1e-3 * rms).all())
