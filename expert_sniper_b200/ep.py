@@ -33,7 +33,7 @@ import torch
 import torch.distributed as dist
 
 from . import _native, hrw
-from .block import MoEBlock, _ptr, _stream
+from .block import MoEBlock, _ptr, _stream, ffn_kernels
 from .config import MoEConfig
 from .quant import PROJS
 
@@ -188,7 +188,14 @@ class CudaEPBackend:
         R, D = x_all.shape
         if self.local is None:  # this rank owns no expert: its partials are zero
             return torch.zeros((R, D), dtype=torch.float32, device=self.device)
-        return self.local.expert_ffn(x_all, idx, w, out_dtype=torch.float32)
+        # Most of the R x k slots are masked (-1: another rank's expert), so
+        # the row count overstates the work per local expert. Each local
+        # expert receives about R k / E_global real pairs, the same per-expert
+        # load as a one-GPU call with R tokens: choose the kernels for that.
+        path = self.local.cfg.kernel_path
+        if path == "auto":
+            path = ffn_kernels(self.cfg, R)
+        return self.local.expert_ffn(x_all, idx, w, out_dtype=torch.float32, kernel_path=path)
 
     def shared(self, x):
         if self.shared_blk is None:
