@@ -38,8 +38,8 @@
 //
 // Warp roles of the persistent CTA (24 warps, one CTA per SM):
 //   warp 0      copies the packed code tiles of each stage into a ring
-//               (raw_full / raw_empty): bulk copies of 2304-byte runs, or
-//               one 5-D TMA load per stage in the small-tile variant
+//               (raw_full / raw_empty): one 5-D TMA load per stage, the
+//               unit's runs of four 576-byte tiles for the stage's groups
 //   warp 1      allocates TMEM; one lane issues tcgen05.mma and commits
 //   warps 2-3   load the B rows into their ring: gate/up gathers token rows
 //               of x16 with cp.async (completion tracked on the ring's
@@ -408,7 +408,7 @@ constexpr int kRun = 4 * kTileBytes;  // four contiguous 576-byte tiles
 //     one per TMEM lane quarter, per K-block; four groups taking K-blocks in
 //     turn) and the MMA reads it from there, so no fp16 weights pass
 //     through shared memory.
-// Rings: raw code tiles (bulk copies, HBM latency) and operand slots, each
+// Rings: raw code tiles (TMA loads, HBM latency) and operand slots, each
 // holding one K-block of A (dequantised weights, written by the dequant
 // warps) and of B (activation rows), completed on one barrier.
 template <bool GU, int NT, bool TA>
