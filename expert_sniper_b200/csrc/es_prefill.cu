@@ -6,8 +6,9 @@
 //     128-byte-swizzled shared memory;
 //   small batches (from 4 pairs per routed expert): 32-token tiles, the
 //     dequantised weights written straight into tensor memory and read
-//     from there by the MMA (A operand in TMEM), two quantisation groups
-//     per pipeline stage, each stage's code tiles fetched with one 5-D TMA.
+//     from there by the MMA (A operand in TMEM), several quantisation
+//     groups per pipeline stage (2 for gate/up, 4 for down: 18 KB of codes
+//     either way).
 //
 // Restates the same math as the decode kernels (engine.py:32-41 gather_qmm
 // gate/up, SwiGLU, gather_qmm down; generate.py:173-178 shared expert), for
@@ -48,10 +49,11 @@
 //   warps 4-7   epilogue: tcgen05.ld from TMEM, math, global stores
 //   warps 8-23  dequantise codes -> fp16 A: large tiles, two groups of
 //               eight warps take alternate stages, one 16-row block per warp
-//               (st.shared in the swizzled layout); small tiles, two groups
-//               of eight warps, one per (TMEM lane quarter, quantisation
-//               group of the stage), one weight row per thread
-//               (tcgen05.st)
+//               (st.shared in the swizzled layout); small tiles, one warp
+//               per (TMEM lane quarter, quantisation group of the stage),
+//               one weight row per thread (tcgen05.st) -- gate/up two groups
+//               of eight warps taking alternate stages, down all sixteen
+//               warps on every stage
 // Every wait is bounded (ES_DEVERR_TIMEOUT); on a timeout each role stops,
 // copies in flight are waited for, and TMEM is freed before returning.
 #include <cudaTypedefs.h>
