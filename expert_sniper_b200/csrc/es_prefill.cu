@@ -406,12 +406,12 @@ constexpr int kRun = 4 * kTileBytes;  // four contiguous 576-byte tiles
 //     into 128-byte-swizzled shared memory by eight warps per K-block (one
 //     16-row block each), two groups taking alternate K-blocks;
 //   TA = true (small batches): token tiles of NT = 32; A is dequantised
-//     into TENSOR MEMORY (tcgen05.st, one weight row per thread: four warps,
-//     one per TMEM lane quarter, per K-block; four groups taking K-blocks in
-//     turn) and the MMA reads it from there, so no fp16 weights pass
-//     through shared memory.
+//     into TENSOR MEMORY (tcgen05.st, one weight row per thread: one warp
+//     per TMEM lane quarter and quantisation group of the stage, kDqGroups
+//     groups of such warps taking stages in turn) and the MMA reads it from
+//     there, so no fp16 weights pass through shared memory.
 // Rings: raw code tiles (TMA loads, HBM latency) and operand slots, each
-// holding one K-block of A (dequantised weights, written by the dequant
+// holding one stage of A (dequantised weights, written by the dequant
 // warps) and of B (activation rows), completed on one barrier.
 template <bool GU, int NT, bool TA>
 struct PfCfg {
