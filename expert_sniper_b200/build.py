@@ -49,21 +49,43 @@ def needs_build() -> bool:
     return any(os.path.getmtime(f) > t for f in _inputs())
 
 
-def build(force: bool = False, verbose: bool = False, extra=None) -> str:
-    if not force and not needs_build():
-        return LIB_PATH
-    cmd = [nvcc_path(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared",
-           "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
-           f"-I{INCLUDE}", f"-I{CSRC}", "--expt-relaxed-constexpr",
-           "-DES_BUILD_LIB", *(extra or []), *sources(), "-o", LIB_PATH + ".tmp"]
+def _flags(extra=None):
+    return [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+            "-Xcompiler", "-fvisibility=hidden", f"-I{INCLUDE}", f"-I{CSRC}",
+            "--expt-relaxed-constexpr", "-DES_BUILD_LIB", *(extra or [])]
+
+
+def _run(cmd, verbose):
     if verbose:
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)
-        raise RuntimeError(f"nvcc failed building {LIB_NAME}")
+        raise RuntimeError(f"nvcc failed: {' '.join(cmd[-3:])}")
     if verbose and (res.stdout or res.stderr):
         sys.stderr.write(res.stdout + res.stderr)
+
+
+def build(force: bool = False, verbose: bool = False, extra=None) -> str:
+    """Compile every .cu file to an object (in parallel, under _build/) and
+    link them into libes_moe.so."""
+    if not force and not needs_build():
+        return LIB_PATH
+    from concurrent.futures import ThreadPoolExecutor
+    obj_dir = os.path.join(PKG_DIR, "_build")
+    os.makedirs(obj_dir, exist_ok=True)
+    nvcc = nvcc_path()
+    objs = []
+    cmds = []
+    for src in sources():
+        obj = os.path.join(obj_dir, os.path.basename(src)[:-3] + ".o")
+        objs.append(obj)
+        cmds.append([nvcc, *_flags(extra), "-c", src, "-o", obj])
+    with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+        for f in [ex.submit(_run, c, verbose) for c in cmds]:
+            f.result()
+    _run([nvcc, *ARCH, "-shared", "-Xcompiler", "-fPIC", *objs,
+          "-o", LIB_PATH + ".tmp"], verbose)
     os.replace(LIB_PATH + ".tmp", LIB_PATH)
     return LIB_PATH
 

@@ -110,6 +110,11 @@ struct Workspace {
   int* item_ctr;       // [2] FFN work counters
   int W, P, kk, E1;
   size_t bytes;
+  // regions the kernels expect at zero when a call starts (they leave them
+  // at zero when a call completes): the error block and control words from
+  // `err`, the token bitmaps (tensor-core path: slot counters) from
+  // `bitmap`, the split-K arrival counters from `counters`
+  size_t zero_ctl_bytes, zero_bitmap_bytes, zero_counter_bytes;
 };
 
 // Carve (or, with base == nullptr, just size) the workspace for T tokens.
@@ -161,6 +166,9 @@ inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
   const size_t cnt_gu = A * (I / 32), cnt_dn = A * (D / 64);
   size_t o_cnt = take((cnt_gu > cnt_dn ? cnt_gu : cnt_dn) * 4);
   w.bytes = off;
+  w.zero_ctl_bytes = o_bitmap - o_err;
+  w.zero_bitmap_bytes = (size_t)E1 * W * 4;
+  w.zero_counter_bytes = (cnt_gu > cnt_dn ? cnt_gu : cnt_dn) * 4;
   w.W = W;
   w.P = P;
   w.kk = kk;

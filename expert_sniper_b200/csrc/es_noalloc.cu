@@ -13,16 +13,23 @@
 // Limits and behaviour:
 //   - the scratch is kNoallocScratchBytes (64 MiB); a call whose workspace
 //     (es_moe_workspace_bytes) would exceed it returns ES_ERR_WORKSPACE;
-//   - the first call on each device looks up the array's device address
-//     (cudaGetSymbolAddress, with that device current); make that first call
-//     before any stream capture on the device;
+//   - the first call in each CUDA context looks up the array's device
+//     address (cudaGetSymbolAddress, with that context's device current) and
+//     caches it keyed by the context: a __device__ array's address belongs
+//     to the context the module was loaded in, so a host that switches to
+//     its own driver-API context, or resets the device, gets the address
+//     resolved again rather than a stale one; make the first call in a
+//     context before any stream capture on its device;
 //   - every call on a device shares the one array and leaves its contents
 //     there; the counters that must start at zero are cleared at the start of
 //     each call, so calls that overlap on the GPU (different streams, or
 //     different host threads) race -- order them on one stream;
 //   - device-side error flags land in the shared scratch and are not
 //     reported by this entry point;
+//   - the counters are cleared with three cudaMemsetAsync calls per call
+//     (a few microseconds of launch work ahead of the block's kernels);
 //   - nothing here calls cudaMalloc, cudaFree or any allocating routine.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -33,25 +40,61 @@
 namespace {
 
 constexpr size_t kNoallocScratchBytes = size_t(64) << 20;
-constexpr int kMaxDevices = 64;
+constexpr int kMaxContexts = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
 
-std::mutex g_setup_mu;
-void* g_scratch_ptr[kMaxDevices] = {};
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
 
-// Device address of the scratch array on the current device (set up once).
-es_status scratch_on_current_device(void** out) {
+// cuCtxGetCurrent from the driver, looked up once through the runtime.
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
+
+std::mutex g_setup_mu;
+CUcontext g_ctx[kMaxContexts] = {};
+void* g_scratch_ptr[kMaxContexts] = {};
+int g_n_ctx = 0;
+
+// Device address of the scratch array in the current context (resolved once
+// per context, after making sure a context is current on this thread).
+es_status scratch_in_current_context(void** out) {
+  // a thread that has not touched the runtime yet has no current context:
+  // cudaSetDevice makes the device's primary context current (it allocates
+  // nothing)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return ES_ERR_CUDA;
-  if (dev < 0 || dev >= kMaxDevices) return ES_ERR_UNSUPPORTED;
-  std::lock_guard<std::mutex> lock(g_setup_mu);
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return ES_ERR_CUDA;
-    g_scratch_ptr[dev] = p;
+  CtxGetCurrentFn get = ctx_get_current();
+  if (!get) return ES_ERR_CUDA;
+  CUcontext ctx = nullptr;
+  if (get(&ctx) != CUDA_SUCCESS) return ES_ERR_CUDA;
+  if (!ctx) {
+    if (cudaSetDevice(dev) != cudaSuccess) return ES_ERR_CUDA;
+    if (get(&ctx) != CUDA_SUCCESS || !ctx) return ES_ERR_CUDA;
   }
-  *out = g_scratch_ptr[dev];
+  std::lock_guard<std::mutex> lock(g_setup_mu);
+  for (int i = 0; i < g_n_ctx; ++i)
+    if (g_ctx[i] == ctx) {
+      *out = g_scratch_ptr[i];
+      return ES_OK;
+    }
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return ES_ERR_CUDA;
+  // a full table (more contexts than kMaxContexts over the process's life)
+  // recycles the oldest entry: a context seen again is simply resolved again
+  const int slot = g_n_ctx < kMaxContexts ? g_n_ctx++ : 0;
+  g_ctx[slot] = ctx;
+  g_scratch_ptr[slot] = p;
+  *out = p;
   return ES_OK;
 }
 
@@ -71,24 +114,17 @@ es_status es_moe_forward_noalloc(const es_moe_cfg* cfg, const void* x, const voi
   if (need > kNoallocScratchBytes) return ES_ERR_WORKSPACE;
   if (T == 0) return ES_OK;
   void* ws = nullptr;
-  if ((s = scratch_on_current_device(&ws)) != ES_OK) return s;
+  if ((s = scratch_in_current_context(&ws)) != ES_OK) return s;
   // zero what the kernels expect at zero (the error word, the front-end
   // ticket and work counters, the token bitmaps, the split-K counters): a
-  // previous call that stopped early could have left them set
+  // previous call that stopped early could have left them set. The region
+  // sizes come from the workspace carving itself.
   const es::Workspace w = es::carve_workspace(ws, cfg->hidden, cfg->num_experts, cfg->top_k,
                                               cfg->inter, cfg->shared_inter > 0, T);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const size_t ctl = reinterpret_cast<char*>(w.bitmap) - reinterpret_cast<char*>(w.err);
-  const size_t bitmap_bytes = (size_t)w.E1 * w.W * 4;
-  const long long routed = (long long)T * cfg->top_k < cfg->num_experts
-                               ? (long long)T * cfg->top_k
-                               : cfg->num_experts;
-  const size_t A = (size_t)(routed + (cfg->shared_inter > 0 ? 1 : 0));
-  const size_t cnt_gu = A * (cfg->inter / 32), cnt_dn = A * (cfg->hidden / 64);
-  const size_t counter_bytes = (cnt_gu > cnt_dn ? cnt_gu : cnt_dn) * 4;
-  if (cudaMemsetAsync(w.err, 0, ctl, st) != cudaSuccess ||
-      cudaMemsetAsync(w.bitmap, 0, bitmap_bytes, st) != cudaSuccess ||
-      cudaMemsetAsync(w.counters, 0, counter_bytes, st) != cudaSuccess)
+  if (cudaMemsetAsync(w.err, 0, w.zero_ctl_bytes, st) != cudaSuccess ||
+      cudaMemsetAsync(w.bitmap, 0, w.zero_bitmap_bytes, st) != cudaSuccess ||
+      cudaMemsetAsync(w.counters, 0, w.zero_counter_bytes, st) != cudaSuccess)
     return ES_ERR_CUDA;
   return es_moe_forward(cfg, x, logits, logits_dtype, cache_bias, shared_gate_w, packed, out,
                         out_dtype, topk_idx, topk_w, T, ws, kNoallocScratchBytes, stream);

@@ -426,20 +426,36 @@ struct PfCfg {
   static constexpr int kABytes = kM * 128;  // one projection (shared-memory A)
   static constexpr int kAStage = TA ? 0 : kProj * kABytes;
   static constexpr int kBStage = kKG * NT * 128;  // one 128-byte-swizzled [NT x 64] block per group
-  static constexpr int kRawStages = TA ? 8 : (GU ? 3 : 6);
-  static constexpr int kOpStages = TA ? 3 : (GU ? 4 : 6);  // A and B share barriers
+  static constexpr int kRawStages = TA ? 8 : (GU ? 4 : 6);
+  static constexpr int kOpStages = TA ? 3 : (GU ? 3 : 6);  // A and B share barriers
   // warps per stage: small-tile variant, one per (TMEM lane quarter, group
   // of the stage); otherwise one per 16-row block
   static constexpr int kNumDqWarps = TA ? 4 * kKG : 8;
-  // groups of kNumDqWarps taking stages in turn. A group waits on a slot's
-  // empty barrier for the stage kOpStages before its own; with more groups
-  // than slots it could run two phases ahead of that barrier, where parity
-  // waits cannot tell the phases apart -- so at most kOpStages groups work
-  // (the gate/up small-tile kernel: 3 slots, 3 groups, the last 4 warps idle)
+  // groups of kNumDqWarps taking stages in turn (stage q goes to group
+  // q mod kDqGroups). Two rules keep every parity wait of a group on the
+  // phase it means:
+  //   - operand slots: a group waits on a slot's empty barrier for the stage
+  //     kOpStages before its own; with more groups than slots it could run
+  //     two phases ahead of that barrier, where parity waits alias -- so at
+  //     most kOpStages groups work;
+  //   - raw slots: slot s is reused every kRawStages stages, and that reuse
+  //     must stay inside one group (kRawStages a multiple of kDqGroups).
+  //     Otherwise a group reaching stage q could test raw_full of a slot
+  //     whose previous phase (stage q - kRawStages, another group's) has not
+  //     landed yet; TMA loads of different slots may land out of order, so
+  //     the parity test would pass on the old phase and read stale codes.
+  // Resulting groups and slots: large gate/up 2 groups of 8 warps (one
+  // 16-row block each), 4 raw slots (group 0 owns slots 0 and 2, group 1
+  // slots 1 and 3), 3 operand slots; large down 2 groups of 8, 6 raw slots
+  // (0, 2, 4 / 1, 3, 5), 6 operand slots; small gate/up 2 groups of 8
+  // (TMEM lane quarter x 2 quantisation groups of the stage), 8 raw slots
+  // (even / odd), 3 operand slots; small down 1 group of 16 (lane quarter x
+  // 4 quantisation groups), all 8 raw and 3 operand slots.
   static constexpr int kDqGroups =
       kDqWarps / kNumDqWarps < kOpStages ? kDqWarps / kNumDqWarps : kOpStages;
   static_assert(!TA || kNumDqWarps * kDqGroups <= kDqWarps, "dequant warps");
   static_assert(kDqGroups <= kOpStages && kDqGroups >= 1, "dequant groups vs operand slots");
+  static_assert(kRawStages % kDqGroups == 0, "each raw slot is reused by one dequant group");
   static constexpr size_t kRawRing = (size_t)kRawStages * kRawBytes;
   static constexpr int kAccCols = kProj * NT;
   static constexpr int kACols = TA ? kKG * kProj * (kGroup / 2) : 0;  // TMEM A columns per slot

@@ -30,7 +30,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="checkout of the reference project (read, never copied)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(args.reference, "src"))
     sys.dont_write_bytecode = True

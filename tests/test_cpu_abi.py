@@ -50,7 +50,8 @@ def test_packed_bytes_equal_reference_block_bytes(lib, name):
     cfg = PRESETS[name]
     nb = _native.packed_bytes(cfg.to_c())
     assert nb == cfg.packed_bytes
-    # the reference's per-expert block bytes (SURVEY byte table / download.py)
+    # the reference's per-expert block bytes: align16K of the nine tensors of
+    # TENSOR_ORDER (src/mlx_expert_sniper/download.py:73-77, 197-212)
     per = {"olmoe-1b-7b": 3538944, "qwen3-30b-a3b": 2654208, "qwen3-next-80b-a3b": 1769472,
            "qwen3-235b-a22b": 10616832}[name]
     assert cfg.bytes_per_expert == per
