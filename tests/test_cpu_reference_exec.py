@@ -1,0 +1,108 @@
+"""The oracle against the reference's own MoE-block code.
+
+tests/golden/reference_block.{npz,json} hold outputs of the reference's
+make_forward layer loop (src/mlx_expert_sniper/generate.py:92-187: cache-bias
+mask from the reference's LRUExpertCache, softmax(precise), argpartition
+top-k, renormalisation, shared expert) and run_expert_ffn
+(src/mlx_expert_sniper/engine.py:15-42), executed unmodified on the MLX
+stand-in (tests/mlx_standin) by tests/golden/make_reference_vectors.py.
+
+Bars, as max |oracle - reference| / RMS(reference) on the stored rows:
+  * fp16 scales (the configurations' format): 1e-2. Where the reference's
+    arithmetic is fp32 (biased routing: fp32 scores) the oracle agrees to
+    ~2e-6; without a bias the reference rounds its scores (and a shared
+    expert's sigmoid gate) to bf16, which moves it by up to ~8e-3.
+  * bf16 scales (real MLX checkpoints): the reference keeps gate/up, h, the
+    down projection and the weighted sum in bf16, which moves it by up to
+    ~4e-2 from exact arithmetic; bar 5e-2.
+Top-k index sets must agree except at near-ties of the reference's own
+selection keys. With a checkout of the reference present, the reference is
+executed again here and must reproduce the stored vectors.
+"""
+from __future__ import annotations
+
+import functools
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import c_oracle as co
+from oracle import moe_oracle as mo
+from tests import _refexec as rx
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+BAR = {"f16": 1e-2, "bf16": 5e-2}
+
+
+@functools.lru_cache(maxsize=None)
+def _golden():
+    with open(os.path.join(GOLDEN, "reference_block.json")) as f:
+        meta = json.load(f)
+    arrays = dict(np.load(os.path.join(GOLDEN, "reference_block.npz")))
+    return {c["name"]: c for c in meta["cases"]}, arrays
+
+
+@functools.lru_cache(maxsize=2)
+def _inputs(name):
+    case = next(c for c in rx.CASES if c["name"] == name)
+    return case, rx.case_inputs(case)
+
+
+def _oracle_rel(name):
+    meta, arrays = _golden()
+    case, (cfg, lay, x, logits, sg, cb, cached) = _inputs(name)
+    m = meta[name]
+    inds = arrays[f"{name}/inds"]
+    rows = arrays[f"{name}/rows"]
+    ref = arrays[f"{name}/out"]
+    lay_np = {k: v.numpy() for k, v in rx.fp16_layer(lay).items()}
+    lg = logits.float().numpy()
+    cbn = None if cb is None else cb.numpy()
+    ok, _, n_tie, bad = mo.topk_parity(inds, lg, cbn, cfg.top_k)
+    assert ok, f"{name}: the reference's top-k is not a top-k of its own keys at {bad}"
+    assert sorted(m["cached_ids"]) == sorted(cached)
+    z = lg + (cbn[None] if cbn is not None else 0.0)
+    w = np.take_along_axis(mo.softmax_f32(z), inds.astype(np.int64), -1)
+    if cfg.norm_topk_prob:
+        w = w / w.sum(-1, keepdims=True)
+    # the reference's scores are the oracle's weights rounded to its dtype
+    tol_w = 2.0 ** -8 if m["scores_dtype"] == "bfloat16" else 1e-6
+    assert np.abs(w - arrays[f"{name}/scores"]).max() <= tol_w * max(1.0, w.max())
+    sgn = None if sg is None else sg.float().numpy()
+    out = co.expert_ffn(x.float().numpy()[rows], lay_np, inds[rows], w[rows].astype(np.float32),
+                        sgn)
+    rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)))
+    return float(np.abs(out - ref).max()) / rms, m
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in rx.CASES])
+def test_oracle_against_reference_vectors(name):
+    rel, m = _oracle_rel(name)
+    assert rel <= BAR[m["scales"]], f"{name}: oracle {rel:.3e} x RMS from the reference"
+    # the distance recorded when the vectors were made
+    assert abs(rel - m["oracle_block_rel"]) <= 1e-4 + 1e-2 * m["oracle_block_rel"]
+    if m["scores_dtype"] == "float32" and m["scales"] == "f16":
+        assert rel <= 1e-5, f"{name}: fp32 reference path, expected agreement to fp32 rounding"
+
+
+def test_reference_reexecutes_to_the_stored_vectors():
+    """Runs the reference's code again (needs a checkout of the reference:
+    $EXPERT_SNIPER_REFERENCE or `reference/` beside this repository)."""
+    root = rx.reference_root()
+    if root is None:
+        pytest.skip("no checkout of the reference project")
+    meta, arrays = _golden()
+    with rx.reference_modules(root) as mods:
+        for name in ("qwen3_30b_T8_bias_f16", "qwen3_30b_T8_bf16"):
+            case, (cfg, lay, x, logits, sg, cb, cached) = _inputs(name)
+            rec = rx.run_reference_block(mods, cfg, lay, x, logits, sg, case.get("bias", 0.0),
+                                         cached)
+            assert np.array_equal(rec["inds"], arrays[f"{name}/inds"])
+            rows = arrays[f"{name}/rows"]
+            ref = arrays[f"{name}/out"]
+            rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)))
+            assert np.abs(rec["out"][rows] - ref).max() <= 1e-6 * rms
+            assert rec["out_dtype"] == meta[name]["out_dtype"]
+            assert rec["scores_dtype"] == meta[name]["scores_dtype"]
