@@ -10,7 +10,9 @@ Reference call surface this mirrors:
   * the shared expert add, generate.py:173-178
 
 `MoEBlock` is the fast path: a layer's experts are repacked once into the
-device layout and every call is one C-ABI call (es_moe_forward). The module
+device layout and every call is one C-ABI call (es_moe_forward), made
+through the registered PyTorch operator torch.ops.expert_sniper.moe_forward_out
+(ops.py). The module
 level `run_expert_ffn` keeps the reference's per-call signature (a dict of
 active experts) for drop-in use; it re-stacks the experts it is given on
 every call, exactly like the reference's stack_proj.
@@ -24,7 +26,8 @@ import ctypes
 import torch
 
 from . import _native
-from .config import MoEConfig
+from . import ops  # noqa: F401  (registers torch.ops.expert_sniper.*)
+from .config import KERNEL_PATHS, MoEConfig
 from .quant import PROJS
 
 _DT_CODE = {torch.bfloat16: _native.ES_DTYPE_BF16, torch.float32: _native.ES_DTYPE_F32}
@@ -204,10 +207,11 @@ class MoEBlock:
             idx = torch.empty((T, cfg.top_k), dtype=torch.int32, device=self.device)
             w = torch.empty((T, cfg.top_k), dtype=torch.float32, device=self.device)
         bias = None if cache_bias is None else cache_bias.to(self.device, torch.float32).contiguous()
-        _native.check("es_moe_forward", _native.lib().es_moe_forward(
-            ctypes.byref(self.ccfg), xf.data_ptr(), lg.data_ptr(), _DT_CODE[lg.dtype], _ptr(bias),
-            _ptr(self.shared_gate_w), self.packed.data_ptr(), out.data_ptr(), _DT_CODE[out.dtype],
-            _ptr(idx), _ptr(w), T, self._ws.data_ptr(), self._ws.numel(), _stream(self.device)))
+        # the registered operator (ops.py) runs es_moe_forward
+        torch.ops.expert_sniper.moe_forward_out(
+            xf, lg, bias, self.packed, self.shared_gate_w, self._ws, out, idx, w,
+            cfg.num_experts, cfg.top_k, cfg.inter, cfg.norm_topk_prob, cfg.shared_inter,
+            KERNEL_PATHS[cfg.kernel_path])
         o = out.reshape(*x.shape[:-1], cfg.hidden)
         if return_routing:
             lead = x.shape[:-1]
@@ -274,6 +278,99 @@ def cache_bias_mask(num_experts: int, cached_ids, bias: float, device="cuda") ->
     return m.to(device)
 
 
+class ExpertPool:
+    """Device-resident packed experts for the run_expert_ffn drop-in.
+
+    The reference hands run_expert_ffn a fresh dict of the active experts'
+    MLX tensors on every call and re-stacks them (engine.py:22-30). Here
+    each distinct expert is repacked once, into a slot of one packed buffer,
+    and a call only maps its expert ids to slots. An expert is identified by
+    the storage, offset, shape and dtype of its nine tensors; the pool keeps
+    a reference to those storages so the memory behind a key cannot be
+    reused for other data while the key is cached. Tensors must not be
+    modified in place after their first call (or call clear()). At most
+    es::kMaxExperts (1024) slots: run_expert_ffn empties a pool that a call
+    would take beyond that."""
+
+    MAX_SLOTS = 1024
+
+    def __init__(self, hidden: int, inter: int, device):
+        self.hidden, self.inter = hidden, inter
+        self.device = torch.device(device)
+        self.cfg1 = MoEConfig(hidden, 1, 1, inter, False, name="pool-slot")
+        self.slot_bytes = self.cfg1.bytes_per_expert
+        self.clear()
+
+    def clear(self):
+        self.buf = None
+        self.capacity = 0
+        self.slots = {}
+        self._keep = []
+        self._ws = None
+
+    @staticmethod
+    def _key(tensors: dict):
+        k = []
+        for proj in PROJS:
+            for kind in ("weight", "scales", "biases"):
+                t = tensors[f"switch_mlp.{proj}.{kind}"]
+                k.append((t.untyped_storage().data_ptr(), t.storage_offset(), tuple(t.shape),
+                          t.dtype))
+        return tuple(k)
+
+    def _grow(self, need: int):
+        cap = max(16, self.capacity)
+        while cap < need:
+            cap *= 2
+        cap = min(cap, self.MAX_SLOTS)
+        buf = torch.empty(cap * self.slot_bytes, dtype=torch.uint8, device=self.device)
+        if self.buf is not None:
+            buf[:self.buf.numel()].copy_(self.buf)
+        self.buf, self.capacity = buf, cap
+
+    def slot(self, tensors: dict) -> int:
+        key = self._key(tensors)
+        s = self.slots.get(key)
+        if s is not None:
+            return s
+        s = len(self.slots)
+        if s >= self.MAX_SLOTS:
+            raise RuntimeError("expert pool full: clear() it first")
+        if s >= self.capacity:
+            self._grow(s + 1)
+        one = {}
+        for proj in PROJS:
+            for kind in ("weight", "scales", "biases"):
+                name = f"switch_mlp.{proj}.{kind}"
+                t = tensors[name]
+                _need_cuda(t, name)
+                one[name] = t.contiguous().unsqueeze(0)
+        dst = self.buf[s * self.slot_bytes:(s + 1) * self.slot_bytes]
+        prepare_packed(self.cfg1, one, out=dst)
+        self._keep.append([tensors[f"switch_mlp.{p}.{k}"].untyped_storage()
+                           for p in PROJS for k in ("weight", "scales", "biases")])
+        self.slots[key] = s
+        return s
+
+    def workspace(self, ccfg, T: int) -> torch.Tensor:
+        need = _native.workspace_bytes(ccfg, T)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+
+_POOLS = {}
+
+
+def expert_pool(hidden: int, inter: int, device) -> ExpertPool:
+    """The process-wide pool for experts of one shape on one device."""
+    dev = torch.device(device)
+    key = (hidden, inter, dev.type, dev.index)
+    if key not in _POOLS:
+        _POOLS[key] = ExpertPool(hidden, inter, dev)
+    return _POOLS[key]
+
+
 def run_expert_ffn(x: torch.Tensor, expert_data: dict, top_k_indices: torch.Tensor,
                    top_k_weights: torch.Tensor) -> torch.Tensor:
     """Drop-in for the reference's run_expert_ffn (engine.py:15-42).
@@ -282,27 +379,41 @@ def run_expert_ffn(x: torch.Tensor, expert_data: dict, top_k_indices: torch.Tens
     CUDA tensor}} for the active experts; indices not in expert_data map to
     the first active expert, as the reference's id_to_local.get(v, 0) does.
     x [..., D] bf16; returns [..., D] in x's dtype.
+
+    Each distinct expert is repacked once into the shape's ExpertPool; a
+    call maps ids to pool slots on the device (no host synchronisation) and
+    runs es_moe_expert_ffn on the pool.
     """
     active = sorted(int(e) for e in expert_data.keys())
     first = expert_data[active[0]]
     I, d8 = first["switch_mlp.gate_proj.weight"].shape
     D = d8 * 8
     k = top_k_indices.shape[-1]
-    U = len(active)
-    cfg = MoEConfig(D, max(U, k), k, I, norm_topk_prob=False)
-    stacked = {}
-    for proj in PROJS:
-        for kind in ("weight", "scales", "biases"):
-            name = f"switch_mlp.{proj}.{kind}"
-            ts = [expert_data[e][name] for e in active]
-            ts += [ts[0]] * (cfg.num_experts - U)   # padding slots, never selected
-            stacked[name] = torch.stack(ts).contiguous()
-    dev = stacked["switch_mlp.gate_proj.weight"].device
-    lut = torch.zeros(max(max(active), int(top_k_indices.max().item())) + 1, dtype=torch.int32,
-                      device=dev)
-    lut[torch.tensor(active, device=dev)] = torch.arange(U, dtype=torch.int32, device=dev)
-    local = lut[top_k_indices.to(dev).long().clamp(min=0)]
-    block = MoEBlock(cfg, weights=stacked, max_tokens=int(x.numel() // D))
-    out = block.expert_ffn(x.to(torch.bfloat16), local, top_k_weights.to(dev, torch.float32),
-                           out_dtype=torch.float32)
-    return out.to(x.dtype)
+    dev = first["switch_mlp.gate_proj.weight"].device
+    pool = expert_pool(D, I, dev)
+    new = sum(pool._key(expert_data[e]) not in pool.slots for e in active)
+    if len(pool.slots) + new > pool.MAX_SLOTS:
+        pool.clear()   # start over so that every expert of this call gets a slot
+    slots = [pool.slot(expert_data[e]) for e in active]
+    hi = active[-1]
+    lut = torch.full((hi + 1,), slots[0], dtype=torch.int32)
+    lut[torch.tensor(active)] = torch.tensor(slots, dtype=torch.int32)
+    lut = lut.to(dev)
+    ids = top_k_indices.to(dev).long()
+    inside = (ids >= 0) & (ids <= hi)
+    local = torch.where(inside, lut[ids.clamp(0, hi)], lut.new_full((), slots[0]))
+    cfg = MoEConfig(D, pool.capacity, k, I, False)   # capacity >= 16 >= k
+    ccfg = cfg.to_c()
+    xf = x.reshape(-1, D).to(torch.bfloat16).contiguous()
+    T = xf.shape[0]
+    idx = local.reshape(T, k).contiguous()
+    w = top_k_weights.to(dev, torch.float32).reshape(T, k).contiguous()
+    out = torch.empty((T, D), dtype=torch.float32, device=dev)
+    ws = pool.workspace(ccfg, T)
+    packed = pool.buf
+    with torch.cuda.device(dev):
+        _native.check("es_moe_expert_ffn", _native.lib().es_moe_expert_ffn(
+            ctypes.byref(ccfg), xf.data_ptr(), idx.data_ptr(), w.data_ptr(), None,
+            packed.data_ptr(), out.data_ptr(), _native.ES_DTYPE_F32, T, ws.data_ptr(),
+            ws.numel(), _stream(dev)))
+    return out.reshape(*x.shape[:-1], D).to(x.dtype)
