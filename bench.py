@@ -60,6 +60,12 @@ def parse_args():
     ap.add_argument("--placement", default="bounded", choices=["hrw", "bounded"],
                     help="--gpus N > 1: expert placement over gpu0..gpuN-1: the reference's "
                          "rendezvous hashing (hrw) or its capacity-bounded variant (bounded)")
+    ap.add_argument("--ep-mode", default="p2p", choices=["p2p", "nccl"],
+                    help="--gpus N > 1: expert-parallel exchange: NVLink peer-to-peer windows "
+                         "(default) or NCCL all_gather + all_to_all")
+    ap.add_argument("--model", default="qwen3-30b-a3b",
+                    choices=["qwen3-30b-a3b", "qwen3-235b-a22b", "olmoe-1b-7b"],
+                    help="--gpus N > 1: layer shape of the expert-parallel workload")
     ap.add_argument("--ep-graphs", action="store_true",
                     help="--gpus N > 1: replay each layer's step (kernels + NCCL collectives) "
                          "as a CUDA graph instead of launching eagerly")
@@ -329,7 +335,7 @@ def run_ours_single(args):
     from expert_sniper_b200.block import ffn_kernels
     from expert_sniper_b200.quant import cache_bias_vector, synthetic_inputs, synthetic_layer
 
-    cfg = PRESETS["qwen3-30b-a3b"].with_(kernel_path=args.kernel_path)
+    cfg = PRESETS[args.model].with_(kernel_path=args.kernel_path)
     dev = torch.device("cuda:0")
     torch.cuda.set_device(dev)
     T, L = args.tokens, args.layers
@@ -484,8 +490,10 @@ def run_ours_single(args):
             rec = json.load(f).get(f"{cfg.name}:T{T}:{r['path']}:{dom}")
         if rec:
             traffic = rec["dram_bytes"] * r["kb"][dom] / rec["algorithmic_bytes"]
+    metric = METRIC if args.model == "qwen3-30b-a3b" else \
+        f"MoE-layer decode tokens/s ({args.model}-shaped 4-bit layer)"
     line = {
-        "metric": METRIC, "value": T / (r["ms"] * 1e-3), "unit": UNIT, "n_gpus": 1,
+        "metric": metric, "value": T / (r["ms"] * 1e-3), "unit": UNIT, "n_gpus": 1,
         "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": r["ms"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4xbf16->f32",
         "data": "synthetic (seeded; random-init 4-bit MLX-affine experts)",
@@ -539,11 +547,16 @@ def run_ours_single(args):
 
 
 def run_ours_ep(args):
-    """N GPUs, one process each: the same Qwen3-30B-A3B-shaped layer with its
-    experts sharded by rendezvous hashing over gpu0..gpu{N-1}; every rank
-    keeps a decode batch of --tokens home tokens (weak scaling: N x T tokens
-    per step), NCCL all_gather / all_to_all move activations, masks and fp32
-    partials. Timed with CUDA events, max over ranks."""
+    """N GPUs, one process each, experts sharded by rendezvous hashing over
+    gpu0..gpu{N-1} (or its capacity-bounded variant). Every rank keeps
+    --tokens home tokens (weak scaling: N x T tokens per step). The default
+    exchange (--ep-mode p2p) is this library's NVLink peer-to-peer path:
+    rows go straight into their owners' exchange windows and partials
+    straight back (es_ep_dispatch / receive / return / combine_p2p), with no
+    collective library on the data path and no host synchronisation; each
+    layer's whole step is one CUDA graph. --ep-mode nccl runs the earlier
+    all_gather + all_to_all exchange. Timed with CUDA events, max over ranks;
+    NCCL is used only for barriers and the max outside the timed region."""
     from datetime import timedelta
 
     import torch
@@ -556,67 +569,77 @@ def run_ours_ep(args):
     local_rank = int(os.environ.get("LOCAL_RANK", str(rank)))
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    cfg = PRESETS["qwen3-30b-a3b"]
+    cfg = PRESETS[args.model]
     T, L = args.tokens, max(2, args.layers)
     pl = ep.make_placement(cfg.num_experts, world, args.placement)
     lcfg = cfg.with_(num_experts=max(1, max(pl.counts)))
-    ws = MoEBlock.new_workspace(lcfg, world * T, dev)
     bias = cache_bias_vector(cfg.num_experts, 0.5, 0)[0].to(dev)
+    p2p = args.ep_mode == "p2p"
+    wins = ep.EpWindows(world, rank, T, cfg.hidden, cfg.top_k, dev) if p2p else None
+    ws = MoEBlock.new_workspace(lcfg, world * T, dev)
     backends, xs, lgs, touched = [], [], [], []
+    t_setup = time.time()
     for l in range(L):
         lay = synthetic_layer(cfg, seed=1000 + l, device=dev)
-        backends.append(ep.CudaEPBackend(cfg, pl, rank, layer=lay, max_tokens=T, device=dev,
-                                         workspace=ws))
+        if p2p:
+            backends.append(ep.P2PEPBackend(cfg, pl, rank, wins, layer=lay,
+                                            local_workspace=ws))
+        else:
+            backends.append(ep.CudaEPBackend(cfg, pl, rank, layer=lay, max_tokens=T, device=dev,
+                                             workspace=ws))
         del lay
         x, _, lg, _ = synthetic_inputs(cfg, T, seed=100_000 * rank + l, device=dev)
         xs.append(x)
         lgs.append(lg)
+    torch.cuda.synchronize()
     torch.cuda.empty_cache()
+    setup_s = time.time() - t_setup
     # experts this rank reads per layer: owned and chosen by any rank's token
     for l in range(L):
-        idx, _ = backends[l].route(lgs[l], bias)
+        b = backends[l]
+        if p2p:
+            b.route(lgs[l], bias)
+            idx = b.idx[:T]
+        else:
+            idx, _ = b.route(lgs[l], bias)
         sel = torch.zeros(cfg.num_experts, dtype=torch.int32, device=dev)
         sel[idx.long().flatten()] = 1
         dist.all_reduce(sel, op=dist.ReduceOp.MAX)
-        owned = torch.tensor(pl.owned[rank], dtype=torch.long, device=dev) \
-            if pl.owned[rank] else torch.zeros(0, dtype=torch.long, device=dev)
-        touched.append(int(sel[owned].sum()) if len(pl.owned[rank]) else 0)
+        owned = pl.owned[rank]
+        touched.append(int(sel[torch.tensor(owned, dtype=torch.long, device=dev)].sum())
+                       if owned else 0)
 
     def step(s):
-        return ep.ep_forward(backends[s % L], xs[s % L], lgs[s % L], bias)
+        b = backends[s % L]
+        if p2p:
+            return b.step(xs[s % L], lgs[s % L], bias)
+        return ep.ep_forward(b, xs[s % L], lgs[s % L], bias)
 
     W = max(3, args.warmup)
     K = args.steps
     stream = torch.cuda.Stream(dev)
     stream.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(stream):
-        for s in range(max(W, L)):   # warm every layer (and NCCL) before capture
+        for s in range(max(W, L)):   # warm every layer before capture
             step(s)
     torch.cuda.synchronize()
     dist.barrier()
-    # one CUDA graph per layer holding the whole exchange (kernels and NCCL
-    # collectives); every rank must end up on the same path
-    graphs, note = [], "each layer's step (kernels + NCCL collectives) is a CUDA graph"
-    if args.ep_graphs:
-        try:
-            with torch.cuda.stream(stream):
-                for l in range(L):
-                    g = torch.cuda.CUDAGraph()
-                    with torch.cuda.graph(g, stream=stream):
-                        step(l)
-                    graphs.append(g)
-            ok = torch.ones(1, device=dev)
-        except Exception as exc:  # reported in the line, never silent
-            graphs, ok = [], torch.zeros(1, device=dev)
-            note = f"graph capture failed ({type(exc).__name__}); eager launches"
+    graphs = []
+    use_graphs = p2p or args.ep_graphs
+    if use_graphs:
+        with torch.cuda.stream(stream):
+            for l in range(L):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    step(l)
+                graphs.append(g)
         torch.cuda.synchronize()
-        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-        if float(ok.item()) < 1:
-            graphs = []
-            note = note if "failed" in note else "graph capture failed on a peer; eager launches"
-    else:
-        note = "eager launches (NCCL collectives not graph-captured; --ep-graphs captures them)"
+        dist.barrier()
+    note = ("p2p exchange over NVLink peer memory (CUDA IPC windows), one CUDA graph per "
+            "layer step" if p2p else
+            ("NCCL all_gather + all_to_all, " + ("CUDA graphs" if graphs else "eager launches")))
 
     def timed(s):
         if graphs:
@@ -630,6 +653,8 @@ def run_ours_ep(args):
     torch.cuda.synchronize()
     dist.barrier()
     clocks = ClockSampler(local_rank).start() if rank == 0 else None
+    if clocks:
+        time.sleep(0.3)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -644,6 +669,37 @@ def run_ours_ep(args):
     clk = clocks.stop() if clocks else None
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms.item())
+    err = wins.read_error() if p2p else 0
+    # per-phase device times of one eager step on every rank (max over ranks)
+    phases = None
+    if p2p:
+        names = ["route", "dispatch", "receive", "expert_ffn", "return", "combine"]
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        acc = torch.zeros(len(names), device=dev)
+        n_rep = min(L, 8)
+        torch.cuda.synchronize()
+        dist.barrier()
+        with torch.cuda.stream(stream):
+            for s in range(n_rep):
+                b = backends[s % L]
+                evs[0].record(stream)
+                b.route(lgs[s % L], bias)
+                evs[1].record(stream)
+                b.dispatch(xs[s % L], T)
+                evs[2].record(stream)
+                b.receive()
+                evs[3].record(stream)
+                b.ffn()
+                evs[4].record(stream)
+                b.ret()
+                evs[5].record(stream)
+                b.combine(b.shared(xs[s % L], T), T)
+                evs[6].record(stream)
+                evs[6].synchronize()
+                acc += torch.tensor([evs[i].elapsed_time(evs[i + 1]) for i in range(len(names))],
+                                    device=dev)
+        dist.all_reduce(acc, op=dist.ReduceOp.MAX)
+        phases = {n: float(v) / n_rep for n, v in zip(names, acc.tolist())}
     # e2e: host buffers in, host buffer out, through the same public path
     xs_h = [x.cpu().pin_memory() for x in xs]
     lg_h = [g.cpu().pin_memory() for g in lgs]
@@ -652,23 +708,29 @@ def run_ours_ep(args):
     K2 = min(K, 500)
     torch.cuda.synchronize()
     dist.barrier()
-    e0.record()
-    for s in range(K2):
-        xd.copy_(xs_h[s % L], non_blocking=True)
-        ld.copy_(lg_h[s % L], non_blocking=True)
-        o = ep.ep_forward(backends[s % L], xd, ld, bias)
-        out_h.copy_(o, non_blocking=True)
-    e1.record()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for s in range(K2):
+            xd.copy_(xs_h[s % L], non_blocking=True)
+            ld.copy_(lg_h[s % L], non_blocking=True)
+            b = backends[s % L]
+            o = b.step(xd, ld, bias) if p2p else ep.ep_forward(b, xd, ld, bias)
+            out_h.copy_(o, non_blocking=True)
+        e1.record(stream)
     e1.synchronize()
     e2e_ms = torch.tensor([e0.elapsed_time(e1) / K2], device=dev)
     dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     per_gpu_bytes = torch.tensor([statistics.mean(touched) * cfg.bytes_per_expert], device=dev)
     dist.all_reduce(per_gpu_bytes, op=dist.ReduceOp.MAX)
+    errs = torch.tensor([float(err)], device=dev)
+    dist.all_reduce(errs, op=dist.ReduceOp.MAX)
     if rank == 0:
         peak, peak_kind = measured_peaks()
         achieved = float(per_gpu_bytes.item()) / (ms * 1e-3) / 1e9
         line = {
-            "metric": METRIC, "value": world * T / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+            "metric": METRIC if args.model == "qwen3-30b-a3b" else
+            f"MoE-layer decode tokens/s ({args.model}-shaped 4-bit layer, expert-parallel)",
+            "value": world * T / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "u4xbf16->f32",
             "data": "synthetic (seeded; random-init 4-bit MLX-affine experts)",
@@ -677,7 +739,7 @@ def run_ours_ep(args):
                                    f"routing bias +0.5, {L} rotating layers",
                        "model": cfg.name, "tokens_per_gpu": T, "global_batch": world * T,
                        "parallelism": f"ep{world}", "placement": args.placement,
-                       "experts_per_gpu": pl.counts,
+                       "exchange": args.ep_mode, "experts_per_gpu": pl.counts,
                        "l2": f"working set {L} layers x {cfg.packed_bytes / world / 1e6:.0f} MB "
                              "per GPU > L2"},
             "roofline": {"bound": "hbm", "kernel": "whole step (max over GPUs of expert bytes)",
@@ -686,15 +748,24 @@ def run_ours_ep(args):
             "e2e": {"value": world * T / (float(e2e_ms.item()) * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": T * (cfg.hidden + cfg.num_experts) * 2,
                     "d2h_bytes_per_step": T * cfg.hidden * 2},
-            "gpu_launches": 7 * K,
+            # p2p: route, dispatch, receive, front, gate/up, down, combine (FFN:
+            # front + 2 GEMMs + combine, or front + scatter + 2 + combine on the
+            # tensor-core kernels), return, combine_p2p
+            "gpu_launches": (10 if p2p else 7) * K,
+            "phase_ms": phases,
+            "device_error": int(errs.item()),
             "clocks": clk,
             "cpu_baseline": None,
+            "setup_s": setup_s,
             "note": note,
         }
         print(json.dumps(line), flush=True)
-    del graphs  # graphs holding NCCL calls go before the process group
+    del graphs
     torch.cuda.synchronize()
+    dist.barrier()
     del backends
+    if wins is not None:
+        wins.close()
     dist.barrier()
     dist.destroy_process_group()
 
@@ -705,7 +776,7 @@ def run_reference(args):
     if rank != 0:
         return
     from expert_sniper_b200 import PRESETS
-    cfg = PRESETS["qwen3-30b-a3b"]
+    cfg = PRESETS[args.model]
     T = args.tokens
     per_step = max(1.0, min(10.0, 60.0 / max(1, args.steps + args.warmup)))
     base = cpu_baseline(cfg, T, per_step * (args.steps + args.warmup))

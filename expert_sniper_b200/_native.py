@@ -39,6 +39,15 @@ class CMlxLayer(ctypes.Structure):
                 ("shared_down_proj", CMlxProj)]
 
 
+class CEpPlan(ctypes.Structure):
+    """Mirror of `es_ep_plan` in include/es_moe.h."""
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("cap", ctypes.c_int32),
+                ("hidden", ctypes.c_int32), ("top_k", ctypes.c_int32),
+                ("num_experts", ctypes.c_int32), ("owner", ctypes.c_void_p),
+                ("local_id", ctypes.c_void_p), ("peers", ctypes.c_void_p),
+                ("window", ctypes.c_void_p), ("err", ctypes.c_void_p)]
+
+
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _SZ = ctypes.c_size_t
@@ -60,6 +69,16 @@ _SIGNATURES = {
                                             _I32, _P, _SZ, _P, _P, _I32]),
     "es_ep_mask": (ctypes.c_int, [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P, _P]),
     "es_ep_combine": (ctypes.c_int, [_P, _P, _I32, _I32, _I32, _P, _I32, _P]),
+    "es_ep_window_bytes": (ctypes.c_int, [_I32, _I32, _I32, _I32, ctypes.POINTER(_SZ)]),
+    "es_ep_window_alloc": (ctypes.c_int, [_SZ, ctypes.POINTER(_P), _P]),
+    "es_ep_window_open": (ctypes.c_int, [_P, ctypes.POINTER(_P)]),
+    "es_ep_window_close": (ctypes.c_int, [_P]),
+    "es_ep_window_free": (ctypes.c_int, [_P]),
+    "es_ep_dispatch": (ctypes.c_int, [ctypes.POINTER(CEpPlan), _P, _P, _P, _I32, _P]),
+    "es_ep_receive": (ctypes.c_int, [ctypes.POINTER(CEpPlan), _P, _P, _P]),
+    "es_ep_rows_offset": (ctypes.c_int, [ctypes.POINTER(CEpPlan), ctypes.POINTER(_SZ)]),
+    "es_ep_return": (ctypes.c_int, [ctypes.POINTER(CEpPlan), _P, _P]),
+    "es_ep_combine_p2p": (ctypes.c_int, [ctypes.POINTER(CEpPlan), _P, _P, _I32, _P, _I32, _P]),
     "es_moe_forward_noalloc": (ctypes.c_int, [_CFG, _P, _P, _I32, _P, _P, _P, _P, _I32, _P, _P,
                                               _I32, _P]),
     "es_moe_read_error": (ctypes.c_int, [_P, _I32, ctypes.POINTER(ctypes.c_uint32), _P]),

@@ -78,7 +78,7 @@ __host__ __device__ inline int nib_pos(int i) {
   return (i & ~7) | (((i & 3) << 1) | ((i >> 2) & 1));
 }
 
-inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+__host__ __device__ inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 // Device pointers carved from the caller's workspace for a call with T tokens.
 struct Workspace {
@@ -198,6 +198,62 @@ inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
     w.y_pair = reinterpret_cast<float*>(b + o_y);
     w.partials = reinterpret_cast<float*>(b + o_part);
     w.counters = reinterpret_cast<int*>(b + o_cnt);
+  }
+  return w;
+}
+
+// Expert-parallel exchange window of one rank (es_ep_*): device memory
+// that the other ranks of the box map (CUDA IPC) and write into directly
+// over NVLink. Every rank carves the same layout, so a rank finds a peer's
+// fields from the peer's base pointer. Written by peers: flags_in, cnt_in,
+// rows_in, tok_in, idx_in, w_in (one region per source rank) and flags_ret,
+// ret_in (one region per owner rank). Local only: epoch and tickets.
+struct EpWindow {
+  uint32_t* epoch;     // [1]   steps completed by this rank
+  int* tickets;        // [3 * world] CTA tickets of dispatch / return / combine
+  uint32_t* flags_in;  // [world] step whose rows source s has delivered
+  uint32_t* flags_ret; // [world] step whose partials owner d has delivered
+  int32_t* cnt_in;     // [world] rows source s sent in its last step
+  uint16_t* rows_in;   // [world][cap][D] bf16 activation rows, by source
+  int32_t* tok_in;     // [world][cap] home token of each row
+  int32_t* idx_in;     // [world][cap][k] local expert ids (-1: not ours)
+  float* w_in;         // [world][cap][k] routing weights
+  float* ret_in;       // [world][cap][D] fp32 partials of my tokens, by owner
+  size_t bytes;
+};
+
+__host__ __device__ inline EpWindow carve_ep_window(void* base, int world, int cap, int D, int k) {
+  EpWindow w{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  const size_t rows = (size_t)world * cap;
+  size_t o_epoch = take(4);
+  size_t o_tk = take((size_t)3 * world * 4);
+  size_t o_fin = take((size_t)world * 4);
+  size_t o_fret = take((size_t)world * 4);
+  size_t o_cnt = take((size_t)world * 4);
+  size_t o_rows = take(rows * D * 2);
+  size_t o_tok = take(rows * 4);
+  size_t o_idx = take(rows * k * 4);
+  size_t o_w = take(rows * k * 4);
+  size_t o_ret = take(rows * D * 4);
+  w.bytes = off;
+  if (base) {
+    char* b = static_cast<char*>(base);
+    w.epoch = reinterpret_cast<uint32_t*>(b + o_epoch);
+    w.tickets = reinterpret_cast<int*>(b + o_tk);
+    w.flags_in = reinterpret_cast<uint32_t*>(b + o_fin);
+    w.flags_ret = reinterpret_cast<uint32_t*>(b + o_fret);
+    w.cnt_in = reinterpret_cast<int32_t*>(b + o_cnt);
+    w.rows_in = reinterpret_cast<uint16_t*>(b + o_rows);
+    w.tok_in = reinterpret_cast<int32_t*>(b + o_tok);
+    w.idx_in = reinterpret_cast<int32_t*>(b + o_idx);
+    w.w_in = reinterpret_cast<float*>(b + o_w);
+    w.ret_in = reinterpret_cast<float*>(b + o_ret);
   }
   return w;
 }

@@ -47,9 +47,11 @@
 //               mbarrier), down copies consecutive pair rows of h16 with
 //               one TMA tile load per quantisation group
 //   warps 4-7   epilogue: tcgen05.ld from TMEM, math, global stores
-//   warps 8-23  dequantise codes -> fp16 A: large tiles, two groups of
-//               eight warps take alternate stages, one 16-row block per warp
-//               (st.shared in the swizzled layout); small tiles, one warp
+//   warps 8-23  dequantise codes -> fp16 A: large tiles, gate/up all
+//               sixteen warps on every stage, one per (16-row block,
+//               projection), down two groups of eight warps taking alternate
+//               stages, one 16-row block per warp (st.shared in the swizzled
+//               layout); small tiles, one warp
 //               per (TMEM lane quarter, quantisation group of the stage),
 //               one weight row per thread (tcgen05.st) -- gate/up two groups
 //               of eight warps taking alternate stages, down all sixteen
@@ -426,11 +428,14 @@ struct PfCfg {
   static constexpr int kABytes = kM * 128;  // one projection (shared-memory A)
   static constexpr int kAStage = TA ? 0 : kProj * kABytes;
   static constexpr int kBStage = kKG * NT * 128;  // one 128-byte-swizzled [NT x 64] block per group
-  static constexpr int kRawStages = TA ? 8 : (GU ? 4 : 6);
-  static constexpr int kOpStages = TA ? 3 : (GU ? 3 : 6);  // A and B share barriers
+  static constexpr int kRawStages = TA ? 8 : (GU ? 3 : 6);
+  static constexpr int kOpStages = TA ? 3 : (GU ? 4 : 6);  // A and B share barriers
+  // projections each large-tile dequant warp converts: gate/up splits them
+  // (one warp per (16-row block, projection)), down has one
+  static constexpr int kPW = (!TA && GU) ? 1 : kProj;
   // warps per stage: small-tile variant, one per (TMEM lane quarter, group
-  // of the stage); otherwise one per 16-row block
-  static constexpr int kNumDqWarps = TA ? 4 * kKG : 8;
+  // of the stage); otherwise one per (16-row block, projection share)
+  static constexpr int kNumDqWarps = TA ? 4 * kKG : 8 * (kProj / kPW);
   // groups of kNumDqWarps taking stages in turn (stage q goes to group
   // q mod kDqGroups). Two rules keep every parity wait of a group on the
   // phase it means:
@@ -444,9 +449,9 @@ struct PfCfg {
   //     whose previous phase (stage q - kRawStages, another group's) has not
   //     landed yet; TMA loads of different slots may land out of order, so
   //     the parity test would pass on the old phase and read stale codes.
-  // Resulting groups and slots: large gate/up 2 groups of 8 warps (one
-  // 16-row block each), 4 raw slots (group 0 owns slots 0 and 2, group 1
-  // slots 1 and 3), 3 operand slots; large down 2 groups of 8, 6 raw slots
+  // Resulting groups and slots: large gate/up 1 group of 16 warps (one per
+  // 16-row block and projection), 3 raw and 4 operand slots; large down 2
+  // groups of 8 (one 16-row block each), 6 raw slots
   // (0, 2, 4 / 1, 3, 5), 6 operand slots; small gate/up 2 groups of 8
   // (TMEM lane quarter x 2 quantisation groups of the stage), 8 raw slots
   // (even / odd), 3 operand slots; small down 1 group of 16 (lane quarter x
@@ -953,7 +958,9 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
     if (!ok) { if (lane == 0) set_error(a.err, 0x8u); set_abort(); }
   } else if (!TA && warp >= kWarpDq0) {
     // ---------------- codes -> fp16 A tiles in shared memory ----------------
-    const int dw = (warp - kWarpDq0) % C::kNumDqWarps;  // 16-row block of the unit
+    const int dwi = (warp - kWarpDq0) % C::kNumDqWarps;
+    const int dw = dwi % 8;                              // 16-row block of the unit
+    const int pj0 = (dwi / 8) * C::kPW;                  // first projection it converts
     const int grp = (warp - kWarpDq0) / C::kNumDqWarps;  // takes K-blocks q = grp mod kDqGroups
     const int g = lane >> 2, c = lane & 3;
     int q = 0;
@@ -967,11 +974,12 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
           ok = false;
           break;
         }
-        uint4 cw[C::kProj];
-        uint2 sbv[C::kProj];
+        uint4 cw[C::kPW];
+        uint2 sbv[C::kPW];
 #pragma unroll
-        for (int pj = 0; pj < C::kProj; ++pj) {
-          const uint8_t* tile = raw + (size_t)sr * C::kRawBytes + (dw * C::kProj + pj) * kTileBytes;
+        for (int pj = 0; pj < C::kPW; ++pj) {
+          const uint8_t* tile =
+              raw + (size_t)sr * C::kRawBytes + (dw * C::kProj + pj0 + pj) * kTileBytes;
           cw[pj] = ld_shared16(tile + 16 * lane);
           sbv[pj] = ld_shared8(tile + kTileCodeBytes + 8 * g);
         }
@@ -984,8 +992,8 @@ __global__ void __launch_bounds__(kThreads, 1) pf_gemm_kernel(const __grid_const
         }
         if (aborted()) { ok = false; break; }
 #pragma unroll
-        for (int pj = 0; pj < C::kProj; ++pj) {
-          uint8_t* at = sa + (size_t)s_a * C::kAStage + pj * C::kABytes;
+        for (int pj = 0; pj < C::kPW; ++pj) {
+          uint8_t* at = sa + (size_t)s_a * C::kAStage + (pj0 + pj) * C::kABytes;
           // rows g and g + 8 of this 16-row block; sbv = (scale, bias) of each
           const __half2 s_lo = __half2half2(__ushort_as_half((uint16_t)(sbv[pj].x & 0xffffu)));
           const __half2 b_lo = __half2half2(__ushort_as_half((uint16_t)(sbv[pj].x >> 16)));

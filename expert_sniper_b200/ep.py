@@ -213,3 +213,228 @@ class CudaEPBackend:
             partials.data_ptr(), _ptr(extra), world, T, D, out.data_ptr(), code,
             _stream(self.device)))
         return out
+
+
+# --------------------------------------------------------------------------- #
+# peer-to-peer exchange over NVLink (es_ep_dispatch / receive / return /
+# combine_p2p): no collective library on the data path
+# --------------------------------------------------------------------------- #
+
+def _check(fn: str, status: int):
+    _native.check(fn, status)
+
+
+class EpWindows:
+    """This rank's exchange window and the mapped windows of every peer.
+
+    The window is allocated once per rank (es_ep_window_alloc) and shared by
+    all layers: the exchange of one layer step completes before the next
+    step writes into it. Handles are swapped once with all_gather_object
+    over the process group (world > 1); every later exchange is plain
+    stores into peer memory made by the kernels."""
+
+    def __init__(self, world: int, rank: int, cap: int, hidden: int, top_k: int, device,
+                 group=None, handles=None, local_only: bool = False):
+        """local_only: ranks emulated in one process on one device; no
+        handles are swapped or opened, and set_peers() supplies the other
+        windows' addresses."""
+        self.world, self.rank, self.cap = world, rank, cap
+        self.hidden, self.top_k = hidden, top_k
+        self.device = torch.device(device)
+        L = _native.lib()
+        nb = ctypes.c_size_t(0)
+        _check("es_ep_window_bytes", L.es_ep_window_bytes(world, cap, hidden, top_k,
+                                                          ctypes.byref(nb)))
+        self.bytes = nb.value
+        ptr = ctypes.c_void_p(0)
+        handle = (ctypes.c_char * 64)()
+        with torch.cuda.device(self.device):
+            _check("es_ep_window_alloc", L.es_ep_window_alloc(nb.value, ctypes.byref(ptr), handle))
+        self.ptr = ptr.value
+        self.handle = bytes(handle)
+        if local_only:
+            handles = None
+        elif handles is None:
+            handles = [self.handle]
+            if world > 1:
+                handles = [None] * world
+                dist.all_gather_object(handles, self.handle, group=group)
+        self.opened = []
+        peers = []
+        with torch.cuda.device(self.device):
+            for r in range(world):
+                if r == rank or local_only:
+                    peers.append(self.ptr if r == rank else 0)
+                    continue
+                p = ctypes.c_void_p(0)
+                buf = (ctypes.c_char * 64).from_buffer_copy(handles[r])
+                _check("es_ep_window_open", L.es_ep_window_open(buf, ctypes.byref(p)))
+                peers.append(p.value)
+                self.opened.append(p.value)
+        self.peers = torch.tensor(peers, dtype=torch.int64, device=self.device)
+        self.err = torch.zeros(64, dtype=torch.int32, device=self.device)
+        self._rows_offset()
+
+    def set_peers(self, ptrs):
+        """Use these window addresses as the peers (ranks emulated in one
+        process on one device, whose windows need no IPC mapping)."""
+        self.peers.copy_(torch.tensor(ptrs, dtype=torch.int64))
+
+    def _rows_offset(self):
+        L = _native.lib()
+        off = ctypes.c_size_t(0)
+        _check("es_ep_rows_offset", L.es_ep_rows_offset(ctypes.byref(self.plan(None, None, 1)),
+                                                        ctypes.byref(off)))
+        self.rows_ptr = self.ptr + off.value
+
+    def plan(self, owner: torch.Tensor, local_id: torch.Tensor, num_experts: int):
+        return _native.CEpPlan(self.world, self.rank, self.cap, self.hidden, self.top_k,
+                               num_experts, _ptr(owner) or self.peers.data_ptr(),
+                               _ptr(local_id) or self.peers.data_ptr(), self.peers.data_ptr(),
+                               self.ptr, self.err.data_ptr())
+
+    def read_error(self, clear: bool = True) -> int:
+        v = int(self.err[0].item())
+        if clear:
+            self.err.zero_()
+        return v & 0xFFFFFFFF
+
+    def close(self):
+        """Unmap the peers' windows and free this rank's. Every rank must be
+        past its last exchange (synchronise and barrier first)."""
+        L = _native.lib()
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            for p in self.opened:
+                L.es_ep_window_close(p)
+            self.opened = []
+            if self.ptr:
+                L.es_ep_window_free(self.ptr)
+                self.ptr = 0
+
+
+class P2PEPBackend:
+    """One rank's MoE layer with expert parallelism over NVLink peer memory.
+
+    step(x, logits, cache_bias):
+      es_moe_route -> es_ep_dispatch (rows to their owners' windows) ->
+      es_ep_receive -> es_moe_expert_ffn (local experts on received rows) ->
+      es_ep_return (partials to their home windows) -> shared expert (home) ->
+      es_ep_combine_p2p (rank-ordered sum).
+    Replaces the reference's per-layer HTTP exchange
+    (src/expert_network/reader.py:237-292, node.py:142-172). All launches
+    go to the current stream, so a whole step can be captured in one CUDA
+    graph; nothing synchronises the host."""
+
+    def __init__(self, cfg: MoEConfig, placement: Placement, rank: int, windows: EpWindows,
+                 layer: dict = None, shared_gate_w: torch.Tensor = None,
+                 out_dtype=torch.bfloat16, kernel_path: str = "auto",
+                 local_workspace: torch.Tensor = None):
+        self.cfg = cfg
+        self.pl = placement
+        self.rank = rank
+        self.world = placement.world
+        self.win = windows
+        self.device = windows.device
+        self.cap = windows.cap
+        self.out_dtype = out_dtype
+        self.route_ccfg = cfg.with_(shared_inter=0).to_c()
+        self.owner = torch.tensor(placement.owner, dtype=torch.int32, device=self.device)
+        self.local_id = torch.tensor(placement.local_id, dtype=torch.int32, device=self.device)
+        self.plan = windows.plan(self.owner, self.local_id, cfg.num_experts)
+        owned = placement.owned[rank]
+        self.n_local = len(owned)
+        R = self.world * self.cap
+        self.local = None
+        if self.n_local:
+            path = kernel_path if kernel_path != "auto" else ffn_kernels(cfg, R)
+            lcfg = cfg.with_(num_experts=self.n_local, shared_inter=0, kernel_path=path,
+                             name=f"{cfg.name}:ep{rank}")
+            w = None if layer is None else {k: v.to(self.device) for k, v in
+                                            shard_layer(layer, owned).items()
+                                            if k.startswith("switch_mlp.")}
+            self.local = MoEBlock(lcfg, weights=w, max_tokens=R, workspace=local_workspace)
+        self.shared_blk = None
+        if cfg.has_shared:
+            sw = {}
+            for proj in PROJS:
+                for kind in ("weight", "scales", "biases"):
+                    t = layer[f"shared_expert.{proj}.{kind}"].to(self.device)
+                    sw[f"switch_mlp.{proj}.{kind}"] = t.unsqueeze(0).contiguous()
+                    sw[f"shared_expert.{proj}.{kind}"] = t.contiguous()
+            scfg = MoEConfig(cfg.hidden, 1, 1, cfg.inter, False, shared_inter=cfg.inter,
+                             name=f"{cfg.name}:shared")
+            self.shared_blk = MoEBlock(scfg, weights=sw, shared_gate_w=shared_gate_w,
+                                       max_tokens=self.cap)
+            self._none = torch.full((self.cap, 1), -1, dtype=torch.int32, device=self.device)
+            self._zero = torch.zeros((self.cap, 1), dtype=torch.float32, device=self.device)
+            self.extra = torch.empty((self.cap, cfg.hidden), dtype=torch.float32,
+                                     device=self.device)
+        k = cfg.top_k
+        self.idx = torch.empty((self.cap, k), dtype=torch.int32, device=self.device)
+        self.w = torch.empty((self.cap, k), dtype=torch.float32, device=self.device)
+        self.ridx = torch.empty((R, k), dtype=torch.int32, device=self.device)
+        self.rw = torch.empty((R, k), dtype=torch.float32, device=self.device)
+        self.y = torch.zeros((R, cfg.hidden), dtype=torch.float32, device=self.device)
+        self.out = torch.empty((self.cap, cfg.hidden), dtype=out_dtype, device=self.device)
+
+    # each phase on the current stream
+    def route(self, logits, cache_bias):
+        T = logits.shape[0]
+        code = _native.ES_DTYPE_F32 if logits.dtype == torch.float32 else _native.ES_DTYPE_BF16
+        _check("es_moe_route", _native.lib().es_moe_route(
+            ctypes.byref(self.route_ccfg), logits.data_ptr(), code, _ptr(cache_bias), T,
+            self.idx.data_ptr(), self.w.data_ptr(), _stream(self.device)))
+
+    def dispatch(self, x, T):
+        _check("es_ep_dispatch", _native.lib().es_ep_dispatch(
+            ctypes.byref(self.plan), x.data_ptr(), self.idx.data_ptr(), self.w.data_ptr(), T,
+            _stream(self.device)))
+
+    def receive(self):
+        _check("es_ep_receive", _native.lib().es_ep_receive(
+            ctypes.byref(self.plan), self.ridx.data_ptr(), self.rw.data_ptr(),
+            _stream(self.device)))
+
+    def ffn(self):
+        if self.local is None:   # no expert here: no token ever sends a row
+            return
+        blk = self.local
+        R = self.world * self.cap
+        _check("es_moe_expert_ffn", _native.lib().es_moe_expert_ffn(
+            ctypes.byref(blk.ccfg), self.win.rows_ptr, self.ridx.data_ptr(), self.rw.data_ptr(),
+            None, blk.packed.data_ptr(), self.y.data_ptr(), _native.ES_DTYPE_F32, R,
+            blk.workspace.data_ptr(), blk.workspace.numel(), _stream(self.device)))
+
+    def ret(self):
+        _check("es_ep_return", _native.lib().es_ep_return(
+            ctypes.byref(self.plan), self.y.data_ptr(), _stream(self.device)))
+
+    def shared(self, x, T):
+        if self.shared_blk is None:
+            return None
+        self.shared_blk.expert_ffn(x, self._none[:T], self._zero[:T], out_dtype=torch.float32,
+                                   out=self.extra[:T])
+        return self.extra
+
+    def combine(self, extra, T):
+        code = _native.ES_DTYPE_F32 if self.out_dtype == torch.float32 else _native.ES_DTYPE_BF16
+        _check("es_ep_combine_p2p", _native.lib().es_ep_combine_p2p(
+            ctypes.byref(self.plan), self.idx.data_ptr(), _ptr(extra), T, self.out.data_ptr(),
+            code, _stream(self.device)))
+        return self.out[:T]
+
+    def step(self, x: torch.Tensor, logits: torch.Tensor, cache_bias=None) -> torch.Tensor:
+        """One layer for this rank's T home tokens (T <= cap; x [T, D] bf16
+        contiguous, logits [T, E]). Every rank of the group must call step
+        for the same layer in the same order."""
+        T = x.shape[0]
+        if T > self.cap or T < 1:
+            raise ValueError(f"1 <= T <= {self.cap}")
+        self.route(logits, cache_bias)
+        self.dispatch(x, T)
+        self.receive()
+        self.ffn()
+        self.ret()
+        extra = self.shared(x, T)
+        return self.combine(extra, T)

@@ -247,6 +247,71 @@ ES_API es_status es_ep_combine(const float* partials, const float* extra,
                                int32_t world, int32_t T, int32_t D, void* out,
                                int32_t out_dtype, es_stream_t stream);
 
+/* ---- peer-to-peer exchange over NVLink (no collective library on the data
+ * path). Each rank owns an exchange window (es_ep_window_*) that every other
+ * rank of the box maps through CUDA IPC. Per layer step, in stream order:
+ *   es_moe_route        home rank: top-k of its own tokens
+ *   es_ep_dispatch      home rank: for every destination rank, the tokens
+ *                       with at least one slot owned there, packed in token
+ *                       order (bf16 row, token id, local expert ids or -1,
+ *                       weights), written into that rank's window; then a
+ *                       step flag
+ *   es_ep_receive       owner rank: waits for every source's flag and lists
+ *                       the received rows' routing for es_moe_expert_ffn
+ *   es_moe_expert_ffn   owner rank: its experts on the received rows
+ *   es_ep_return        owner rank: each row's fp32 partial written back
+ *                       into its home rank's window, then a step flag
+ *   es_ep_combine_p2p   home rank: waits for every owner's flag, sums the
+ *                       partials of the owners each token used in rank
+ *                       order (+ extra), advances the step counter
+ * The step counter lives in the window, so a captured CUDA graph of the
+ * whole step replays correctly. Every wait is bounded (about a second):
+ * on timeout the kernel sets ES_DEVERR_TIMEOUT in `err` and returns.
+ * Counterpart of the Expert Network's per-layer HTTP exchange:
+ * src/expert_network/reader.py:237-292 (driver) and node.py:142-198 (node). */
+typedef struct es_ep_plan {
+  int32_t world, rank;
+  int32_t cap;              /* most home tokens per rank and step            */
+  int32_t hidden, top_k, num_experts;
+  const int32_t* owner;     /* [E] device: rank that owns each global expert */
+  const int32_t* local_id;  /* [E] device: index of the expert on its owner  */
+  void* const* peers;       /* [world] device array: every rank's window base
+                             * as mapped in this process (own one at [rank]) */
+  void* window;             /* this rank's window                             */
+  uint32_t* err;            /* device error word (e.g. a workspace's)         */
+} es_ep_plan;
+
+/* Bytes of one rank's exchange window for `world` ranks, `cap` home tokens
+ * per step, hidden size and top-k. */
+ES_API es_status es_ep_window_bytes(int32_t world, int32_t cap, int32_t hidden, int32_t top_k,
+                                    size_t* bytes_out);
+/* Allocate (cudaMalloc) and zero a window of `bytes` on the current device
+ * and export it: *ipc_handle_out receives a 64-byte cudaIpcMemHandle_t. */
+ES_API es_status es_ep_window_alloc(size_t bytes, void** window_out, void* ipc_handle_out);
+/* Map a peer's window from its 64-byte handle (cudaIpcOpenMemHandle). */
+ES_API es_status es_ep_window_open(const void* ipc_handle, void** window_out);
+/* Unmap a peer's window / free this rank's own. */
+ES_API es_status es_ep_window_close(void* peer_window);
+ES_API es_status es_ep_window_free(void* window);
+
+ES_API es_status es_ep_dispatch(const es_ep_plan* plan, const void* x_bf16,
+                                const int32_t* topk_idx, const float* topk_w, int32_t T,
+                                es_stream_t stream);
+/* idx_out / w_out: [world * cap][k] routing of the window's received rows
+ * (rows beyond a source's count: -1 / 0). The rows themselves are
+ * window + es_ep_rows_offset(): [world * cap][hidden] bf16. */
+ES_API es_status es_ep_receive(const es_ep_plan* plan, int32_t* idx_out, float* w_out,
+                               es_stream_t stream);
+ES_API es_status es_ep_rows_offset(const es_ep_plan* plan, size_t* offset_out);
+/* y: [world * cap][hidden] fp32 partials of the received rows. */
+ES_API es_status es_ep_return(const es_ep_plan* plan, const float* y, es_stream_t stream);
+/* out[t] = sum over owners d (rank order) used by token t of the returned
+ * partial (+ extra[t] if extra != NULL), as out_dtype; topk_idx is the home
+ * routing passed to es_ep_dispatch. */
+ES_API es_status es_ep_combine_p2p(const es_ep_plan* plan, const int32_t* topk_idx,
+                                   const float* extra, int32_t T, void* out, int32_t out_dtype,
+                                   es_stream_t stream);
+
 /* es_moe_forward for callers that cannot allocate device memory (a runtime
  * that owns the whole GPU arena, a plugin whose host forbids outside
  * allocations, a loop where cudaMalloc's implicit synchronisation is not
