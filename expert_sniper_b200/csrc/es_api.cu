@@ -40,6 +40,7 @@ es_status check_cfg(const es_moe_cfg* c) {
 // decode below p = 4, 32-token tiles up to p = 48, 128-token tiles above --
 // the crossovers measured on a B200 for the Qwen3-30B and Qwen3-Next layers.
 enum { kFfnDecode = 0, kFfnTensorLarge = 1, kFfnTensorSmall = 2 };
+constexpr long long kFoldScatterSlots = 8192;
 int ffn_variant(const es_moe_cfg* c, int T) {
   if (c->kernel_path == 3) return kFfnTensorSmall;
   if (c->kernel_path == 2) return kFfnTensorLarge;
@@ -103,13 +104,17 @@ es_status run_pf_front(const es_moe_cfg* cfg, const Workspace& w, const es::Rout
   d.cnt = reinterpret_cast<int*>(w.bitmap);  // zero between calls, like the bitmaps
   d.off_e = w.wpre; d.n_active = w.n_active; d.act_e = w.act_e; d.act_off = w.act_off;
   d.act_n = w.act_n; d.ticket = w.ticket; d.item_ctr = w.item_ctr;
+  // up to kFoldScatterSlots slots the front end's last CTA scatters them
+  // itself; larger batches use the grid-wide scatter kernel
+  d.fold_scatter = (long long)T * w.kk <= kFoldScatterSlots;
+  d.pair_tok = w.pair_tok; d.pos_shared = w.pos;
   es::PfScatterArgs sc{};
   sc.cs_pos = w.cs_pos; sc.rank = w.rank; sc.off_e = w.wpre; sc.pair_tok = w.pair_tok;
   sc.pos_shared = w.pos; sc.T = T; sc.E = cfg->num_experts; sc.k = cfg->top_k;
   sc.has_shared = cfg->shared_inter > 0;
   if (mk.mark(0, st) != cudaSuccess) return ES_ERR_CUDA;
   if (es::launch_pf_front(r, d, st) != cudaSuccess) return ES_ERR_CUDA;
-  if (es::launch_pf_scatter(sc, st) != cudaSuccess) return ES_ERR_CUDA;
+  if (!d.fold_scatter && es::launch_pf_scatter(sc, st) != cudaSuccess) return ES_ERR_CUDA;
   return cuda_status(mk.mark(1, st));
 }
 

@@ -96,6 +96,11 @@ struct PfFrontArgs {
   int32_t* act_n;
   int* ticket;              // CTAs done routing (zero between calls)
   int* item_ctr;            // [2] zeroed for symmetry with the decode front end
+  // small batches: the last CTA also turns slots into pair indices (the
+  // work of pf_scatter), saving a launch; pair_tok / pos_shared are written
+  int fold_scatter;
+  int32_t* pair_tok;        // [P]
+  int32_t* pos_shared;      // [T]
 };
 
 struct PfScatterArgs {

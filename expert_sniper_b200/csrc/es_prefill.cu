@@ -233,18 +233,35 @@ ES_DEV float x_hi(uint32_t w, bool f16) {
   return f16 ? __half2float(__ushort_as_half((uint16_t)(w >> 16))) : __uint_as_float(w & 0xffff0000u);
 }
 
-ES_DEV void x_row_to_f16(const uint16_t* xr, uint16_t* outr, float* inv_out, int D, bool f16) {
-  const unsigned full = 0xffffffffu;
+// One pass over the row: the lane's 16-byte chunks (D / 256 of them, at most
+// kMaxRowChunks) are loaded once into registers, then reduced and converted.
+constexpr int kMaxRowChunks = 16;  // D <= 4096
+
+// the lane's chunks of row xr into registers (issued early, used later)
+ES_DEV void x_row_load(const uint16_t* xr, int D, uint4 (&v)[kMaxRowChunks]) {
   const int lane = threadIdx.x & 31;
   const uint4* x4 = reinterpret_cast<const uint4*>(xr);
-  float m = 0.f;
-  for (int c = lane; c < D / 8; c += 32) {
-    const uint4 v = x4[c];
-    const uint32_t ws[4] = {v.x, v.y, v.z, v.w};
+  const int nch = D / 8;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      m = fmaxf(m, fabsf(x_lo(ws[i], f16)));
-      m = fmaxf(m, fabsf(x_hi(ws[i], f16)));
+  for (int i = 0; i < kMaxRowChunks; ++i) {
+    const int c = lane + 32 * i;
+    v[i] = c < nch ? x4[c] : make_uint4(0, 0, 0, 0);
+  }
+}
+
+ES_DEV void x_row_to_f16(const uint4 (&v)[kMaxRowChunks], uint16_t* outr, float* inv_out, int D,
+                         bool f16) {
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const int nch = D / 8;
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxRowChunks; ++i) {
+    const uint32_t ws[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      m = fmaxf(m, fabsf(x_lo(ws[q], f16)));
+      m = fmaxf(m, fabsf(x_hi(ws[q], f16)));
     }
   }
 #pragma unroll
@@ -258,13 +275,15 @@ ES_DEV void x_row_to_f16(const uint16_t* xr, uint16_t* outr, float* inv_out, int
   const float scale = __uint_as_float((uint32_t)(127 + s) << 23);
   if (lane == 0) *inv_out = __uint_as_float((uint32_t)(127 - s) << 23);
   uint4* o4 = reinterpret_cast<uint4*>(outr);
-  for (int c = lane; c < D / 8; c += 32) {
-    const uint4 v = x4[c];
+#pragma unroll
+  for (int i = 0; i < kMaxRowChunks; ++i) {
+    const int c = lane + 32 * i;
+    if (c >= nch) break;
     // elements e0..e7: v.x = (e0, e1), v.y = (e2, e3), v.z = (e4, e5), v.w = (e6, e7)
-    const float e0 = x_lo(v.x, f16) * scale, e1 = x_hi(v.x, f16) * scale;
-    const float e2 = x_lo(v.y, f16) * scale, e3 = x_hi(v.y, f16) * scale;
-    const float e4 = x_lo(v.z, f16) * scale, e5 = x_hi(v.z, f16) * scale;
-    const float e6 = x_lo(v.w, f16) * scale, e7 = x_hi(v.w, f16) * scale;
+    const float e0 = x_lo(v[i].x, f16) * scale, e1 = x_hi(v[i].x, f16) * scale;
+    const float e2 = x_lo(v[i].y, f16) * scale, e3 = x_hi(v[i].y, f16) * scale;
+    const float e4 = x_lo(v[i].z, f16) * scale, e5 = x_hi(v[i].z, f16) * scale;
+    const float e6 = x_lo(v[i].w, f16) * scale, e7 = x_hi(v[i].w, f16) * scale;
     uint4 o;
     o.x = h2_bits(__floats2half2_rn(e0, e4));
     o.y = h2_bits(__floats2half2_rn(e1, e5));
@@ -287,6 +306,10 @@ __global__ void __launch_bounds__(kFrontThreads) pf_front_kernel(RouteArgs r, Pf
   pdl_trigger();
 
   for (int t = blockIdx.x * kFrontWarps + warp; t < r.T; t += gridDim.x * kFrontWarps) {
+    // the token's activation row is loaded first so that its latency overlaps
+    // the routing
+    uint4 xv[kMaxRowChunks];
+    x_row_load(r.x + (size_t)t * r.D, r.D, xv);
     int my_e = -1;
     float my_w = 0.f;
     if (r.logits) {
@@ -309,7 +332,7 @@ __global__ void __launch_bounds__(kFrontThreads) pf_front_kernel(RouteArgs r, Pf
       const float gsg = shared_gate_warp(r.x + (size_t)t * r.D, r.sg_w, r.D, r.x_f16 != 0);
       if (lane == 0) r.sgate[t] = gsg;
     }
-    x_row_to_f16(r.x + (size_t)t * r.D, r.x_perm + (size_t)t * r.D, r.xsum + t, r.D, r.x_f16 != 0);
+    x_row_to_f16(xv, r.x_perm + (size_t)t * r.D, r.xsum + t, r.D, r.x_f16 != 0);
   }
 
   // the last CTA turns the counts into offsets and the active list
@@ -357,6 +380,7 @@ __global__ void __launch_bounds__(kFrontThreads) pf_front_kernel(RouteArgs r, Pf
     if (e >= E1) break;
     const int cnt = s_off[e];
     d.off_e[e] = run_c;
+    s_off[e] = run_c;  // the thread's own experts only: counts become offsets
     if (cnt > 0) {
       d.act_e[run_f] = e;
       d.act_off[run_f] = run_c;
@@ -370,6 +394,26 @@ __global__ void __launch_bounds__(kFrontThreads) pf_front_kernel(RouteArgs r, Pf
     d.item_ctr[0] = 0;
     d.item_ctr[1] = 0;
     *d.ticket = 0;
+  }
+  if (!d.fold_scatter) return;  // kernel-uniform
+  // slot -> pair index, pair -> token (pf_scatter's work) from the offsets in
+  // shared memory; the slots and their ranks come from every CTA
+  __syncthreads();
+  const int nk = r.T * k;
+  for (int i = tid; i < nk; i += kFrontThreads) {
+    const int e = __ldcg(d.cs_pos + i);
+    if (e >= 0) {
+      const int p = s_off[e] + __ldcg(d.rank + i);
+      d.pair_tok[p] = i / k;
+      d.cs_pos[i] = p;
+    }
+  }
+  if (r.has_shared) {
+    for (int t = tid; t < r.T; t += kFrontThreads) {
+      const int p = s_off[E] + t;
+      d.pair_tok[p] = t;
+      d.pos_shared[t] = p;
+    }
   }
 }
 
