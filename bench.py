@@ -211,6 +211,47 @@ def cpu_baseline(cfg, T, seconds, layer_np=None, seed=0):
                       f"(router + experts + combine), median {med * 1e3:.1f} ms/call"}
 
 
+def cpu_baselines_other(seconds):
+    """The C restatement on the host cores for the other configurations'
+    layers (BASELINE: OLMoE T = 1 and 32, Qwen3-Next prefill T = 4096 with
+    the shared expert, Qwen3-235B T = 256 with bias +0.5), each timed for
+    about `seconds` (at least one call); CPU-generated seeded weights."""
+    from expert_sniper_b200 import PRESETS
+    from expert_sniper_b200.quant import cache_bias_vector, synthetic_inputs, synthetic_layer
+    from oracle import c_oracle
+    c_oracle.build()
+    cores = os.cpu_count() or 1
+    out = []
+    cases = [("olmoe-1b-7b", 1, 0.0), ("olmoe-1b-7b", 32, 0.0),
+             ("qwen3-next-80b-a3b", 4096, 0.0), ("qwen3-235b-a22b", 256, 0.5)]
+    layers = {}
+    for name, T, b in cases:
+        cfg = PRESETS[name]
+        if name not in layers:
+            layers.clear()
+            import torch
+            dev = "cuda" if torch.cuda.is_available() else "cpu"
+            layers[name] = {k: v.cpu().numpy()
+                            for k, v in synthetic_layer(cfg, seed=7, device=dev).items()}
+        lay = layers[name]
+        x, _, logits, sg = synthetic_inputs(cfg, T, seed=8)
+        bias = cache_bias_vector(cfg.num_experts, b, 0)[0].numpy() if b > 0 else None
+        xf, lf = x.float().numpy(), logits.float().numpy()
+        sgn = None if sg is None else sg.float().numpy()
+        times = []
+        t_end = time.perf_counter() + seconds
+        while not times or time.perf_counter() < t_end:
+            t0 = time.perf_counter()
+            idx, w = c_oracle.route(lf, bias, cfg.top_k, cfg.norm_topk_prob)
+            c_oracle.expert_ffn(xf, lay, idx, w, sgn, nthreads=cores)
+            times.append(time.perf_counter() - t0)
+        med = statistics.median(times)
+        out.append({"model": name, "tokens": T, "bias": b, "ms_per_call": med * 1e3,
+                    "tokens_per_s": T / med, "calls": len(times), "cores": cores,
+                    "kind": "port"})
+    return out
+
+
 # --------------------------------------------------------------------------- #
 # prefill: Qwen3-Next-80B-A3B layer, T = 4096 (tensor-core path)
 # --------------------------------------------------------------------------- #
@@ -401,6 +442,21 @@ def run_ours_single(args):
             e1.synchronize()
         return e0.elapsed_time(e1) / K
 
+    def step_distribution(graphs, n):
+        """ms of single graph replays, each bracketed by CUDA events on the
+        launching stream (includes the event records' own gap)."""
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(n + 1)]
+        with torch.cuda.stream(stream):
+            torch.cuda.synchronize()
+            evs[0].record(stream)
+            for s in range(n):
+                graphs[s % L].replay()
+                evs[s + 1].record(stream)
+            evs[-1].synchronize()
+        v = sorted(evs[i].elapsed_time(evs[i + 1]) for i in range(n))
+        q = lambda f: v[min(n - 1, int(f * n))]
+        return {"n": n, "p10": q(0.1), "median": q(0.5), "p90": q(0.9)}
+
     def profile_kernels(xs, lgs, outs, K):
         events = []
         for l in range(L):
@@ -437,6 +493,7 @@ def run_ours_single(args):
             time.sleep(0.3)
         ms = time_graphs(graphs, K, W)
         clk = clocks.stop() if clocks else None
+        dist_ms = step_distribution(graphs, min(K, 1000))
         del graphs
         mean_bytes = sum(block_bytes(cfg, Tc, U[s % L]) for s in range(W, W + K)) / K
         prof = profile_kernels(xs, lgs, outs, min(K, 4 * L))
@@ -445,7 +502,8 @@ def run_ours_single(args):
         kb = {k: statistics.mean(kernel_bytes(cfg, Tc, U[l], path_c)[k] for l, _ in prof[k])
               for k in KERNELS}
         results[Tc] = dict(ms=ms, bytes=mean_bytes, U=statistics.mean(U), U_layers=U, kmean=kmean,
-                           kb=kb, clocks=clk, xs=xs, lgs=lgs, outs=outs, path=path_c)
+                           kb=kb, clocks=clk, xs=xs, lgs=lgs, outs=outs, path=path_c,
+                           dist=dist_ms)
 
     # e2e through the public API with host buffers
     r = results[T]
@@ -515,6 +573,7 @@ def run_ours_single(args):
                      "(profiles/traffic.json), scaled by algorithmic bytes to this run's mean",
                      "algorithmic_bytes_per_launch": r["kb"][dom], "launch_ms": r["kmean"][dom]},
         "kernel_ms": r["kmean"],
+        "step_ms_distribution": r["dist"],
         "e2e": {"value": T / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": T * cfg.hidden * 2 + T * cfg.num_experts * 2,
                 "d2h_bytes_per_step": T * cfg.hidden * 2, "ms_per_step": e2e_ms},
@@ -528,7 +587,8 @@ def run_ours_single(args):
                    "value": Tc / (results[Tc]["ms"] * 1e-3),
                    "gbs": results[Tc]["bytes"] / (results[Tc]["ms"] * 1e-3) / 1e9,
                    "frac": results[Tc]["bytes"] / (results[Tc]["ms"] * 1e-3) / 1e9 / peak,
-                   "kernel_ms": results[Tc]["kmean"], "kernel_path": results[Tc]["path"]}
+                   "kernel_ms": results[Tc]["kmean"], "kernel_path": results[Tc]["path"],
+                   "step_ms_distribution": results[Tc]["dist"]}
                   for Tc in sweep],
         "setup_s": setup_s,
     }
@@ -542,7 +602,14 @@ def run_ours_single(args):
         from expert_sniper_b200.decoder import measure as measure_decoder
         del blocks, packed
         torch.cuda.empty_cache()
-        line["decoder"] = measure_decoder((1, 16), 2048, 40, 48)
+        dec = measure_decoder((1, 16), 2048, 40, 48)
+        for res in dec["results"].values():
+            res["roofline"] = {"bound": "hbm", "achieved": res["gbs"], "peak": peak,
+                               "peak_kind": peak_kind, "unit": "GB/s",
+                               "frac": res["gbs"] / peak, "bytes_per_step": res["bytes_per_step"]}
+        line["decoder"] = dec
+    if not args.no_cpu_baseline:
+        line["cpu_baselines"] = cpu_baselines_other(args.cpu_seconds / 3)
     print(json.dumps(line), flush=True)
 
 

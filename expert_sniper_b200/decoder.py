@@ -315,6 +315,51 @@ class Decoder:
         return self.logits
 
 
+def distinct_experts(dec: "Decoder", tokens: torch.Tensor) -> list:
+    """Distinct experts each layer's MoE block selects in one eager step
+    (the step's position is restored afterwards)."""
+    counts = []
+    wrapped = []
+    for L in dec.layers:
+        blk = L["moe"]
+        orig = blk.forward
+
+        def rec(n, logits, bias=None, *a, _blk=blk, _orig=orig, **kw):
+            idx, _ = _blk.route(logits, bias)
+            counts.append(int(torch.unique(idx).numel()))
+            return _orig(n, logits, bias, *a, **kw)
+        blk.forward = rec
+        wrapped.append(blk)
+    p0 = dec.pos.clone()
+    graph, dec.graph = dec.graph, None
+    try:
+        dec.step(tokens)
+        torch.cuda.synchronize()
+    finally:
+        dec.graph = graph
+        dec.pos.copy_(p0)
+        for blk in wrapped:
+            del blk.forward
+    return counts
+
+
+def step_bytes(dec: "Decoder", distinct: list) -> int:
+    """Algorithmic HBM bytes of one decode step: every layer's attention,
+    router and selected experts' weights, the KV cache read up to the
+    position (plus the new row written), embedding rows, final norm and
+    lm_head. `distinct` = distinct experts per layer."""
+    c = dec.dcfg
+    D, H, KV, hd, V = c.hidden, c.heads, c.kv_heads, c.head_dim, c.vocab
+    B = dec.batch
+    ctx = int(dec.pos.item())
+    per_layer = ((H + 2 * KV) * hd * D + D * H * hd + c.moe.num_experts * D) * 2
+    kv = B * KV * (ctx + 1) * hd * 2 * 2
+    total = len(dec.layers) * (per_layer + kv)
+    total += sum(distinct) * c.moe.bytes_per_expert
+    total += V * D * 2 + B * D * 2
+    return int(total)
+
+
 def measure(batches=(1, 16), context: int = 2048, steps: int = 40, layers: int = 48,
             fused: bool = True) -> dict:
     """Decode tokens/s of the Qwen3-30B-shaped decoder: graph replays with
@@ -337,7 +382,11 @@ def measure(batches=(1, 16), context: int = 2048, steps: int = 40, layers: int =
         e1.record()
         e1.synchronize()
         ms = e0.elapsed_time(e1) / steps
-        res[str(B)] = {"ms_per_step": ms, "tokens_per_s": B / (ms * 1e-3), "build_s": build_s}
+        U = distinct_experts(dec, toks)
+        nbytes = step_bytes(dec, U)
+        res[str(B)] = {"ms_per_step": ms, "tokens_per_s": B / (ms * 1e-3), "build_s": build_s,
+                       "bytes_per_step": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9,
+                       "mean_distinct_experts": sum(U) / len(U)}
         del dec
         torch.cuda.empty_cache()
     return {"decoder": dcfg.name, "layers": layers, "context": context, "steps": steps,
