@@ -161,6 +161,10 @@ def kernel_bytes(cfg, T, U, path="decode"):
     kernels keep fp16 rows and x as scaled fp16 with one scale per token."""
     D, I, E, k = cfg.hidden, cfg.inter, cfg.num_experts, cfg.top_k
     P = T * k
+    if path == "fused":
+        # one kernel: the instrumentation puts the whole block in "front"
+        return {"front": block_bytes(cfg, T, U), "gap": 0, "gateup": 0, "down": 0,
+                "combine": 0}
     yb = 4 if path == "decode" else 2
     xprep = T * D * 2 + (T * (D // 64) * 4 if path == "decode" else T * 4)
     return {
@@ -577,9 +581,11 @@ def run_ours_single(args):
         "e2e": {"value": T / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": T * cfg.hidden * 2 + T * cfg.num_experts * 2,
                 "d2h_bytes_per_step": T * cfg.hidden * 2, "ms_per_step": e2e_ms},
-        # per step: decode kernels front, gate/up, down, combine; tensor-core
-        # kernels front, scatter, gate/up, down, combine
-        "gpu_launches": (4 if r["path"] == "decode" else 5) * args.steps,
+        # per step: fused tiny-batch kernel 1; decode kernels front, gate/up,
+        # down, combine; tensor-core kernels front, (scatter above 8192
+        # slots), gate/up, down, combine
+        "gpu_launches": {"fused": 1, "decode": 4}.get(r["path"], 5 if T * cfg.top_k > 8192 else 4)
+        * args.steps,
         "kernel_path": r["path"],
         "clocks": r["clocks"],
         "cpu_baseline": cpu,

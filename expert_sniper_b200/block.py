@@ -88,11 +88,16 @@ def uses_tensor_path(cfg: MoEConfig, T: int) -> bool:
 
 
 def ffn_kernels(cfg: MoEConfig, T: int) -> str:
-    """The expert-FFN kernels a call with T tokens runs ("decode", "tensor"
-    or "tensor-small"): the rule of es_moe_cfg.kernel_path in
-    include/es_moe.h (automatic: by the average pairs per routed expert
-    p = T k / E, decode below 4, 32-token tiles up to 48, 128-token tiles
-    above, tensor-core kernels only from T = 64)."""
+    """The expert-FFN kernels a call with T tokens runs ("fused", "decode",
+    "tensor" or "tensor-small"): the rule of es_moe_cfg.kernel_path in
+    include/es_moe.h (automatic: the fused tiny-batch kernel for T <= 4;
+    otherwise by the average pairs per routed expert p = T k / E, decode
+    below 4, 32-token tiles up to 48, 128-token tiles above, tensor-core
+    kernels only from T = 64)."""
+    fused_fits = (cfg.x_dtype == "bf16" and 1 <= T <= 4 and cfg.hidden <= 4096
+                  and T * cfg.top_k <= 512)
+    if cfg.kernel_path == "fused":
+        return "fused" if fused_fits else "decode"
     if cfg.kernel_path != "auto":
         return cfg.kernel_path
     pk = T * cfg.top_k
@@ -100,7 +105,9 @@ def ffn_kernels(cfg: MoEConfig, T: int) -> str:
         return "tensor"
     if T >= 64 and pk >= 4 * cfg.num_experts:
         return "tensor-small"
-    return "tensor-small" if cfg.x_dtype == "f16" else "decode"
+    if cfg.x_dtype == "f16":
+        return "tensor-small"
+    return "fused" if fused_fits else "decode"
 
 
 class MoEBlock:

@@ -12,7 +12,7 @@ import ctypes
 from dataclasses import dataclass, replace
 
 
-KERNEL_PATHS = {"auto": 0, "decode": 1, "tensor": 2, "tensor-small": 3}
+KERNEL_PATHS = {"auto": 0, "decode": 1, "tensor": 2, "tensor-small": 3, "fused": 4}
 X_DTYPES = {"bf16": 0, "f16": 1}  # es_dtype codes
 
 
@@ -47,8 +47,8 @@ class MoEConfig:
             raise ValueError(f"kernel_path must be one of {sorted(KERNEL_PATHS)}")
         if self.x_dtype not in X_DTYPES:
             raise ValueError(f"x_dtype must be one of {sorted(X_DTYPES)}")
-        if self.x_dtype == "f16" and self.kernel_path == "decode":
-            raise ValueError("the decode kernels read bf16 activations")
+        if self.x_dtype == "f16" and self.kernel_path in ("decode", "fused"):
+            raise ValueError("the decode and fused kernels read bf16 activations")
 
     @property
     def has_shared(self) -> bool:

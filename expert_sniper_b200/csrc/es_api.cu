@@ -26,10 +26,11 @@ es_status check_cfg(const es_moe_cfg* c) {
   if (c->num_experts > es::kMaxExperts) return ES_ERR_UNSUPPORTED;
   if (c->top_k > es::kMaxTopK) return ES_ERR_UNSUPPORTED;
   if (c->shared_inter != 0 && c->shared_inter != c->inter) return ES_ERR_UNSUPPORTED;
-  if (c->kernel_path < 0 || c->kernel_path > 3) return ES_ERR_INVALID_ARG;
+  if (c->kernel_path < 0 || c->kernel_path > 4) return ES_ERR_INVALID_ARG;
   if (c->x_dtype != ES_DTYPE_BF16 && c->x_dtype != ES_DTYPE_F16) return ES_ERR_UNSUPPORTED;
-  // the decode kernels read bf16 activations only
-  if (c->x_dtype == ES_DTYPE_F16 && c->kernel_path == 1) return ES_ERR_UNSUPPORTED;
+  // the decode kernels and the fused tiny-batch kernel read bf16 activations only
+  if (c->x_dtype == ES_DTYPE_F16 && (c->kernel_path == 1 || c->kernel_path == 4))
+    return ES_ERR_UNSUPPORTED;
   return ES_OK;
 }
 
@@ -39,9 +40,13 @@ es_status check_cfg(const es_moe_cfg* c) {
 // average (token, expert) pairs per routed expert p = T k / E (and T >= 64):
 // decode below p = 4, 32-token tiles up to p = 48, 128-token tiles above --
 // the crossovers measured on a B200 for the Qwen3-30B and Qwen3-Next layers.
-enum { kFfnDecode = 0, kFfnTensorLarge = 1, kFfnTensorSmall = 2 };
+enum { kFfnDecode = 0, kFfnTensorLarge = 1, kFfnTensorSmall = 2, kFfnFused = 3 };
 constexpr long long kFoldScatterSlots = 8192;
 int ffn_variant(const es_moe_cfg* c, int T) {
+  const bool fused_fits = c->x_dtype == ES_DTYPE_BF16 &&
+                          es::small_path_fits(T, c->hidden, c->inter, c->num_experts, c->top_k,
+                                              c->shared_inter > 0);
+  if (c->kernel_path == 4) return fused_fits ? kFfnFused : kFfnDecode;
   if (c->kernel_path == 3) return kFfnTensorSmall;
   if (c->kernel_path == 2) return kFfnTensorLarge;
   if (c->kernel_path == 1) return kFfnDecode;  // (fp16 x is rejected with path 1)
@@ -49,7 +54,8 @@ int ffn_variant(const es_moe_cfg* c, int T) {
   if (T >= 64 && pk > 48LL * c->num_experts) return kFfnTensorLarge;
   if (T >= 64 && pk >= 4LL * c->num_experts) return kFfnTensorSmall;
   // fp16 activations are read by the tensor-core kernels only
-  return c->x_dtype == ES_DTYPE_F16 ? kFfnTensorSmall : kFfnDecode;
+  if (c->x_dtype == ES_DTYPE_F16) return kFfnTensorSmall;
+  return (T <= es::kSmallMaxTokens && fused_fits) ? kFfnFused : kFfnDecode;
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -178,6 +184,30 @@ es_status run_ffn(const es_moe_cfg* cfg, const Workspace& w, const void* packed,
   cb.out = out; cb.out_f32 = out_f32;
   if (es::launch_combine(cb, st) != cudaSuccess) return ES_ERR_CUDA;
   return cuda_status(mk.mark(5, st));
+}
+
+// The fused tiny-batch block: one cooperative kernel (es_small.cu). The
+// instrumentation events all land around that one kernel (the whole block
+// shows as the front-end interval).
+es_status run_small(const es_moe_cfg* cfg, const Workspace& w, const es::RouteArgs& r,
+                    const void* packed, void* out, int out_f32, cudaStream_t st,
+                    const Marks& mk) {
+  es::SmallArgs a{};
+  a.logits = r.logits; a.logits_f32 = r.logits_f32; a.bias = r.bias;
+  a.in_idx = r.in_idx; a.in_w = r.in_w; a.x = r.x; a.sg_w = r.sg_w;
+  a.packed = static_cast<const uint8_t*>(packed);
+  a.expert_bytes = es::expert_bytes(cfg->hidden, cfg->inter);
+  a.T = r.T; a.D = cfg->hidden; a.E = cfg->num_experts; a.k = cfg->top_k; a.I = cfg->inter;
+  a.renorm = r.renorm; a.has_shared = r.has_shared;
+  a.out = out; a.out_f32 = out_f32; a.out_idx = r.out_idx; a.out_w = r.out_w;
+  a.part = w.partials; a.h16 = w.h16;
+  // the split-K arrival counters are zero between calls on every path
+  a.bar = reinterpret_cast<unsigned*>(w.counters); a.err = w.err;
+  if (mk.mark(0, st) != cudaSuccess) return ES_ERR_CUDA;
+  if (es::launch_small(a, st) != cudaSuccess) return ES_ERR_CUDA;
+  for (int i = 1; i <= 5; ++i)
+    if (mk.mark(i, st) != cudaSuccess) return ES_ERR_CUDA;
+  return ES_OK;
 }
 
 es_status check_common(const es_moe_cfg* cfg, const void* x, const void* packed,
@@ -347,6 +377,10 @@ es_status es_moe_expert_ffn(const es_moe_cfg* cfg, const void* x, const int32_t*
   r.sgate = w.sgate; r.x_perm = w.x_perm; r.xsum = w.xsum; r.err = w.err;
   Marks mk;
   const int v = ffn_variant(cfg, T);
+  if (v == kFfnFused) {
+    r.out_idx = nullptr; r.out_w = nullptr;
+    return run_small(cfg, w, r, packed, out, out_dtype == ES_DTYPE_F32, st, mk);
+  }
   if (v != kFfnDecode) {
     r.out_idx = nullptr; r.out_w = nullptr;
     es_status s2 = run_pf_front(cfg, w, r, T, st, mk);
@@ -397,6 +431,8 @@ es_status es_moe_forward_timed(const es_moe_cfg* cfg, const void* x, const void*
   r.out_idx = idx; r.out_w = wts;
   r.sgate = w.sgate; r.x_perm = w.x_perm; r.xsum = w.xsum; r.err = w.err;
   const int v = ffn_variant(cfg, T);
+  if (v == kFfnFused)
+    return run_small(cfg, w, r, packed, out, out_dtype == ES_DTYPE_F32, st, mk);
   if (v != kFfnDecode) {
     es_status s2 = run_pf_front(cfg, w, r, T, st, mk);
     if (s2 != ES_OK) return s2;

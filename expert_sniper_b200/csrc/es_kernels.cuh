@@ -132,6 +132,30 @@ struct alignas(64) PfArgs {
   uint32_t* err;
 };
 
+// The fused tiny-batch block (es_small.cu), T <= 4.
+struct SmallArgs {
+  // routing source: logits (+ optional bias) or given top-k
+  const void* logits;
+  int logits_f32;
+  const float* bias;
+  const int32_t* in_idx;    // [T][k] or null
+  const float* in_w;        // [T][k]
+  const uint16_t* x;        // [T][D] bf16
+  const uint16_t* sg_w;     // [D] bf16 shared gate weight or null
+  const uint8_t* packed;
+  size_t expert_bytes;
+  int T, D, E, k, I, renorm, has_shared;
+  int ks_gu, ks_dn;         // K shares of the gate/up and down items
+  void* out;
+  int out_f32;
+  int32_t* out_idx;         // [T][k] or null
+  float* out_w;
+  float* part;              // split-K partial sums (gate/up, then reused by down)
+  uint16_t* h16;            // [P][I] fp16, fragment order
+  unsigned* bar;            // [2] grid-barrier counters, zero between calls
+  uint32_t* err;
+};
+
 struct PrepareArgs {
   // routed experts of projection p (gate, up, down): weight / scales / biases
   // of expert e start at w[p] + e * ew[p] bytes (and likewise s, b), so both
@@ -187,5 +211,9 @@ cudaError_t launch_pf_gateup(const PfArgs& a, long long tokens, int max_units, b
 cudaError_t launch_pf_down(const PfArgs& a, long long pairs, int max_units, bool small,
                            cudaStream_t st);
 cudaError_t launch_prepare(const PrepareArgs& a, cudaStream_t st);
+// fused tiny-batch block: whether a call can take it, and the launch
+constexpr int kSmallMaxTokens = 4;
+bool small_path_fits(int T, int D, int I, int E, int k, int has_shared);
+cudaError_t launch_small(SmallArgs a, cudaStream_t st);
 
 }  // namespace es

@@ -1,0 +1,539 @@
+// The whole MoE block for tiny batches (T <= 4 tokens) in one cooperative
+// kernel: router, gate/up + SwiGLU, down and combine, with three grid-wide
+// barriers between the phases instead of four dependent launches.
+//
+// Restates generate.py:122-136 (router, once per CTA: every CTA routes the
+// few tokens itself, so routing needs no grid-wide hand-off), engine.py:32-41
+// (gather_qmm gate/up, SwiGLU, gather_qmm down, weighted sum) and
+// generate.py:173-178 (shared expert, as one more expert whose per-token
+// weight is the sigmoid gate).
+//
+// Phases (grid = one CTA per SM, all co-resident: cooperative launch):
+//   0  every CTA: route the T tokens (warp per token), list the distinct
+//      experts in ascending id with their (token, weight) pairs, and stage x
+//      in fragment order with 64-group sums in shared memory
+//   1  gate/up: items (expert, 32-row pair of I, K share) spread over all
+//      warps; codes stream from HBM straight into registers (two groups in
+//      flight), one m16n8k16 MMA step per 16 K on the exact 128 + q codes,
+//      scale and bias applied per (row, group) in fp32: w = s q + b with no
+//      weight rounding; each item writes its fp32 partial sums
+//   -- barrier --
+//   2  reduce: items (expert, row pair): the K shares summed in fixed order,
+//      SwiGLU, h rounded once to fp16 (fragment order)
+//   -- barrier --
+//   3  down: items (expert, 64-row quad of D, I share) on fp16 1024 + q codes
+//      and h, partial sums out
+//   -- barrier --
+//   4  combine: each output element sums its token's slots in ascending
+//      expert id (the K shares of each in fixed order), then the shared
+//      expert; bf16 or fp32 out
+// All arithmetic is fixed-order, so results are bitwise repeatable. Every
+// barrier wait is bounded (about a second) and reports ES_DEVERR_TIMEOUT.
+#include <cooperative_groups.h>
+
+#include "es_common.cuh"
+#include "es_kernels.cuh"
+#include "es_route.cuh"
+
+namespace es {
+namespace {
+
+constexpr int kSmWarps = 16;
+constexpr int kSmThreads = kSmWarps * 32;
+constexpr int kSmMaxT = 4;
+constexpr int kSmMaxPairs = kSmMaxT * kMaxTopK + kSmMaxT;  // routed + shared
+constexpr uint32_t kErrTimeout = 0x8u;
+constexpr uint32_t kErrRange = 0x10u;
+
+// Grid barrier b (1, 2, 3) on a counter that is zero when the kernel starts:
+// every CTA adds one and waits for b * gridDim.x arrivals (bounded).
+ES_DEV void grid_barrier(unsigned* bar, unsigned b, uint32_t* err) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(bar, 1u);
+    const unsigned target = b * gridDim.x;
+    const long long t0 = clock64();
+    while (true) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(bar) : "memory");
+      if (v >= target) break;
+      if (clock64() - t0 > (1LL << 31)) {
+        atomicOr(err, kErrTimeout);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// Shared-memory state of one CTA (identical in every CTA after phase 0).
+struct SmallState {
+  int n_pairs, n_act;
+  int act_e[kSmMaxPairs];      // distinct experts, ascending (E = shared)
+  int act_off[kSmMaxPairs];    // their first pair
+  int act_n[kSmMaxPairs];      // their pairs
+  int pair_tok[kSmMaxPairs];   // token of each pair
+  float pair_w[kSmMaxPairs];   // its weight (shared expert: the sigmoid gate)
+  int pair_u[kSmMaxPairs];     // its entry in act_*
+  int slot_e[kSmMaxT * kMaxTopK];
+  float slot_w[kSmMaxT * kMaxTopK];
+  int first[kSmMaxT * kMaxTopK];
+  int tok_n[kSmMaxT];                        // pairs of each token
+  int tok_pair[kSmMaxT * (kMaxTopK + 1)];    // their indices, ascending
+  float sgate[kSmMaxT];
+};
+
+// Phase 0: route the T tokens (warp t routes token t) or read the given
+// routing, and list the pairs in (expert id, token, slot) order.
+template <int VPL>
+ES_DEV void small_route(const SmallArgs& a, SmallState& st) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int k = a.k, T = a.T;
+  if (warp < T) {
+    const int t = warp;
+    int my_e = -1;
+    float my_w = 0.f;
+    if (a.logits) {
+      route_token_warp<VPL>(a.logits, a.logits_f32, a.bias, t, a.E, k, a.renorm,
+                            blockIdx.x == 0 ? a.err : nullptr, my_e, my_w);
+    } else if (lane < k) {
+      my_e = a.in_idx[(size_t)t * k + lane];
+      my_w = a.in_w[(size_t)t * k + lane];
+      if (my_e < -1 || my_e >= a.E) {
+        if (blockIdx.x == 0) set_error(a.err, 0x1u);
+        my_e = -1;
+      }
+    }
+    if (lane < k) {
+      st.slot_e[t * k + lane] = my_e;
+      st.slot_w[t * k + lane] = my_w;
+      if (blockIdx.x == 0 && a.out_idx) {
+        a.out_idx[(size_t)t * k + lane] = my_e;
+        a.out_w[(size_t)t * k + lane] = my_w;
+      }
+    }
+    if (a.has_shared) {
+      const float gs = shared_gate_warp(a.x + (size_t)t * a.D, a.sg_w, a.D);
+      if (lane == 0) st.sgate[t] = gs;
+    }
+  }
+  __syncthreads();
+  // one thread per slot: whether it is the first slot of its expert, then
+  // its rank among the valid slots by (expert, slot index) -- its pair
+  // index -- and, for a first slot, the expert's entry
+  const int ns = T * k;
+  const int s = threadIdx.x;
+  const bool valid = s < ns && st.slot_e[s] >= 0;
+  bool first = valid;
+  if (valid)
+    for (int s2 = 0; s2 < s; ++s2)
+      if (st.slot_e[s2] == st.slot_e[s]) { first = false; break; }
+  if (s < ns) st.first[s] = first ? 1 : 0;
+  const int n_routed = __syncthreads_count(valid);
+  const int n_first = __syncthreads_count(first);
+  if (valid) {
+    const int e = st.slot_e[s];
+    int rank = 0, first_rank = 0, cnt_same = 0;
+    for (int s2 = 0; s2 < ns; ++s2) {
+      const int e2 = st.slot_e[s2];
+      if (e2 < 0) continue;
+      rank += (e2 < e || (e2 == e && s2 < s)) ? 1 : 0;
+      cnt_same += e2 == e;
+      first_rank += (e2 < e && st.first[s2]) ? 1 : 0;
+    }
+    st.pair_tok[rank] = s / k;
+    st.pair_w[rank] = st.slot_w[s];
+    st.pair_u[rank] = first_rank;
+    if (first) {
+      st.act_e[first_rank] = e;
+      st.act_off[first_rank] = rank;
+      st.act_n[first_rank] = cnt_same;
+    }
+  }
+  if (threadIdx.x == 0) {
+    int n_act = n_first, n_pairs = n_routed;
+    if (a.has_shared) {
+      st.act_e[n_act] = a.E;
+      st.act_off[n_act] = n_pairs;
+      st.act_n[n_act] = T;
+      for (int t = 0; t < T; ++t) {
+        st.pair_tok[n_pairs + t] = t;
+        st.pair_w[n_pairs + t] = st.sgate[t];
+        st.pair_u[n_pairs + t] = n_act;
+      }
+      ++n_act;
+      n_pairs += T;
+    }
+    st.n_act = n_act;
+    st.n_pairs = n_pairs;
+    // each token's pairs in ascending pair index = ascending expert id
+    for (int t = 0; t < T; ++t) st.tok_n[t] = 0;
+    for (int p = 0; p < n_pairs; ++p) {
+      const int t = st.pair_tok[p];
+      st.tok_pair[t * (kMaxTopK + 1) + st.tok_n[t]++] = p;
+    }
+  }
+  __syncthreads();
+}
+
+// x rows -> shared memory in fragment order, with 64-group sums
+ES_DEV void small_stage_x(const SmallArgs& a, uint16_t* xs, float* xsum) {
+  const unsigned full = 0xffffffffu;
+  const int chunks = a.D / 8, GD = a.D / kGroup;
+  const int total = a.T * chunks;
+  for (int c0 = 0; c0 < total; c0 += kSmThreads) {
+    const int c = c0 + threadIdx.x;
+    const bool lv = c < total;
+    const int tt = lv ? c / chunks : 0, q8 = lv ? c % chunks : 0;
+    float sum = permute_chunk8(a.x + (size_t)tt * a.D, xs + (size_t)tt * a.D, q8, lv);
+    sum += __shfl_xor_sync(full, sum, 1);
+    sum += __shfl_xor_sync(full, sum, 2);
+    sum += __shfl_xor_sync(full, sum, 4);
+    if (lv && (q8 & 7) == 0) xsum[tt * GD + (q8 >> 3)] = sum;
+  }
+  __syncthreads();
+}
+
+// Phase 1, one item: expert entry u, row pair rp (32 rows of I: two 16-row
+// blocks, gate and up), K share ks of GPI groups. Partial sums per lane:
+// [block j][gate v0..3 | up v0..3] -> part[((u * RP + rp) * KS + ks) * 512].
+ES_DEV void small_gateup_item(const SmallArgs& a, const SmallState& st, const uint16_t* xs,
+                              const float* xsum, int u, int rp, int ks) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int GD = a.D / kGroup, RP = a.I / 32, KS = a.ks_gu, GPI = GD / KS;
+  const int e = st.act_e[u], p0 = st.act_off[u], n = st.act_n[u];
+  const uint8_t* base = a.packed + (size_t)e * a.expert_bytes;
+  const int tb = g < n ? st.pair_tok[p0 + g] : -1;
+  const int tc0 = 2 * c < n ? st.pair_tok[p0 + 2 * c] : -1;
+  const int tc1 = 2 * c + 1 < n ? st.pair_tok[p0 + 2 * c + 1] : -1;
+  float acc[2][8];
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int v = 0; v < 8; ++v) acc[j][v] = 0.f;
+  uint4 cw[2][4];
+  uint2 sb[2][4];
+  auto load = [&](int G, uint4 (&w)[4], uint2 (&b)[4]) {
+    const uint8_t* run = base + gateup_tile_off(GD, 2 * rp, G, 0);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      w[t] = ld_stream16(run + t * kTileBytes + lane * 16);
+      b[t] = __ldg(reinterpret_cast<const uint2*>(run + t * kTileBytes + kTileCodeBytes + g * 8));
+    }
+  };
+  const int G0 = ks * GPI;
+  load(G0, cw[0], sb[0]);
+  for (int i = 0; i < GPI; ++i) {
+    const int G = G0 + i, cur = i & 1;
+    if (i + 1 < GPI) {
+      if (cur == 0) load(G + 1, cw[1], sb[1]);
+      else load(G + 1, cw[0], sb[0]);
+    }
+    // B fragments of the pairs' tokens and their group sums, from shared memory
+    uint32_t bw[8];
+    {
+      uint4 xa = make_uint4(0, 0, 0, 0), xb = xa;
+      if (tb >= 0) {
+        const uint4* xp = reinterpret_cast<const uint4*>(xs + (size_t)tb * a.D + G * kGroup + c * 16);
+        xa = xp[0];
+        xb = xp[1];
+      }
+      bw[0] = xa.x; bw[1] = xa.y; bw[2] = xa.z; bw[3] = xa.w;
+      bw[4] = xb.x; bw[5] = xb.y; bw[6] = xb.z; bw[7] = xb.w;
+    }
+    const float xs0 = tc0 >= 0 ? xsum[tc0 * GD + G] : 0.f;
+    const float xs1 = tc1 >= 0 ? xsum[tc1 * GD + G] : 0.f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int j = t >> 1, proj = t & 1;  // tile order in a run: block, then (gate, up)
+      const uint4 q = cur == 0 ? cw[0][t] : cw[1][t];
+      const uint2 sbv = cur == 0 ? sb[0][t] : sb[1][t];
+      const float s0 = lo_half_f(sbv.x), s8 = lo_half_f(sbv.y);
+      const float b0 = fmaf(-128.f, s0, hi_half_f(sbv.x));
+      const float b8 = fmaf(-128.f, s8, hi_half_f(sbv.y));
+      float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        mma_bf16(tmp, code_pair(q.x, s), code_pair(q.z, s), code_pair(q.y, s),
+                 code_pair(q.w, s), bw[2 * s], bw[2 * s + 1], tmp);
+      float* av = acc[j] + 4 * proj;
+      av[0] = fmaf(s0, tmp[0], fmaf(b0, xs0, av[0]));
+      av[1] = fmaf(s0, tmp[1], fmaf(b0, xs1, av[1]));
+      av[2] = fmaf(s8, tmp[2], fmaf(b8, xs0, av[2]));
+      av[3] = fmaf(s8, tmp[3], fmaf(b8, xs1, av[3]));
+    }
+  }
+  float4* out = reinterpret_cast<float4*>(a.part + ((size_t)(u * RP + rp) * KS + ks) * 512) + lane * 4;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    out[q] = make_float4(acc[q >> 1][(q & 1) * 4 + 0], acc[q >> 1][(q & 1) * 4 + 1],
+                         acc[q >> 1][(q & 1) * 4 + 2], acc[q >> 1][(q & 1) * 4 + 3]);
+}
+
+// Phase 2, one item (u, rp): the K shares summed in order, SwiGLU, h in
+// fp16 (fragment order) for the expert's pairs.
+ES_DEV void small_reduce_item(const SmallArgs& a, const SmallState& st, int u, int rp) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int RP = a.I / 32, KS = a.ks_gu;
+  const int p0 = st.act_off[u], n = st.act_n[u];
+  float v[16];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) v[q] = 0.f;
+  const float4* src = reinterpret_cast<const float4*>(a.part + (size_t)(u * RP + rp) * KS * 512);
+  // the shares in two batches of four, every load of a batch in flight
+  // together; summed in share order
+#pragma unroll
+  for (int k0 = 0; k0 < kMaxSplitK; k0 += 4) {
+    float4 t[4][4];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        t[kk][q] = k0 + kk < KS ? __ldcg(src + (size_t)(k0 + kk) * 128 + lane * 4 + q)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        v[4 * q] += t[kk][q].x; v[4 * q + 1] += t[kk][q].y;
+        v[4 * q + 2] += t[kk][q].z; v[4 * q + 3] += t[kk][q].w;
+      }
+  }
+  uint32_t range = 0;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int rb = 2 * rp + j;
+#pragma unroll
+    for (int vv = 0; vv < 4; ++vv) {
+      const int row = vv < 2 ? g : g + 8;
+      const int col = 2 * c + (vv & 1);
+      if (col < n) {
+        const float gv = v[j * 8 + vv], uv = v[j * 8 + 4 + vv];
+        float h = gv / (1.f + expf(-gv)) * uv;
+        if (!(fabsf(h) <= 65504.f)) { range = 1; h = h != h ? 0.f : copysignf(65504.f, h); }
+        a.h16[(size_t)(p0 + col) * a.I + frag_pos(rb * 16 + row)] = __half_as_ushort(__float2half_rn(h));
+      }
+    }
+  }
+  if (range) set_error(a.err, kErrRange);
+}
+
+// Phase 3, one item: expert entry u, row quad rq (64 rows of D), I share ks
+// of GPI groups. fp16 codes 1024 + q against fp16 h (exact products), scale
+// and bias per (row, group) on the fp32 sums. Partial sums per lane:
+// [block j][v] -> part[((u * RQ + rq) * KS + ks) * 512].
+ES_DEV void small_down_item(const SmallArgs& a, const SmallState& st, int u, int rq, int ks) {
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int GI = a.I / kGroup, RQ = a.D / 64, KS = a.ks_dn, GPI = GI / KS;
+  const int e = st.act_e[u], p0 = st.act_off[u], n = st.act_n[u];
+  const uint8_t* base = a.packed + (size_t)e * a.expert_bytes;
+  float acc[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) acc[j][v] = 0.f;
+  uint4 cw[2][4];
+  uint2 sb[2][4];
+  auto load = [&](int G, uint4 (&w)[4], uint2 (&b)[4]) {
+    const uint8_t* run = base + down_tile_off(a.D, a.I, 4 * rq, G);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      w[t] = ld_stream16(run + t * kTileBytes + lane * 16);
+      b[t] = __ldg(reinterpret_cast<const uint2*>(run + t * kTileBytes + kTileCodeBytes + g * 8));
+    }
+  };
+  const int G0 = ks * GPI;
+  load(G0, cw[0], sb[0]);
+  for (int i = 0; i < GPI; ++i) {
+    const int G = G0 + i, cur = i & 1;
+    if (i + 1 < GPI) {
+      if (cur == 0) load(G + 1, cw[1], sb[1]);
+      else load(G + 1, cw[0], sb[0]);
+    }
+    uint32_t hw[8];
+    {
+      uint4 h0 = make_uint4(0, 0, 0, 0), h1 = h0;
+      if (g < n) {
+        const uint4* hp = reinterpret_cast<const uint4*>(a.h16 + (size_t)(p0 + g) * a.I + G * kGroup + c * 16);
+        h0 = __ldcg(hp);
+        h1 = __ldcg(hp + 1);
+      }
+      hw[0] = h0.x; hw[1] = h0.y; hw[2] = h0.z; hw[3] = h0.w;
+      hw[4] = h1.x; hw[5] = h1.y; hw[6] = h1.z; hw[7] = h1.w;
+    }
+    float hs = 0.f;
+#pragma unroll
+    for (int v = 0; v < 8; ++v) hs += lo_half_f(hw[v]) + hi_half_f(hw[v]);
+    hs += __shfl_xor_sync(full, hs, 1);
+    hs += __shfl_xor_sync(full, hs, 2);
+    const float hs0 = __shfl_sync(full, hs, (2 * c) << 2);
+    const float hs1 = __shfl_sync(full, hs, (2 * c + 1) << 2);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 q = cur == 0 ? cw[0][j] : cw[1][j];
+      const uint2 sbv = cur == 0 ? sb[0][j] : sb[1][j];
+      const float s0 = lo_half_f(sbv.x), s8 = lo_half_f(sbv.y);
+      const float b0 = fmaf(-1024.f, s0, hi_half_f(sbv.x));
+      const float b8 = fmaf(-1024.f, s8, hi_half_f(sbv.y));
+      float tmp[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+        mma_f16(tmp, code_pair_f16(q.x, s), code_pair_f16(q.z, s), code_pair_f16(q.y, s),
+                code_pair_f16(q.w, s), hw[2 * s], hw[2 * s + 1], tmp);
+      acc[j][0] = fmaf(s0, tmp[0], fmaf(b0, hs0, acc[j][0]));
+      acc[j][1] = fmaf(s0, tmp[1], fmaf(b0, hs1, acc[j][1]));
+      acc[j][2] = fmaf(s8, tmp[2], fmaf(b8, hs0, acc[j][2]));
+      acc[j][3] = fmaf(s8, tmp[3], fmaf(b8, hs1, acc[j][3]));
+    }
+  }
+  float4* out = reinterpret_cast<float4*>(a.part + ((size_t)(u * RQ + rq) * KS + ks) * 512) + lane * 4;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) out[j] = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+}
+
+// Phase 4: out[t][d] = sum over the token's pairs (ascending expert id, the
+// shared expert last) of weight x (its down partials summed in share
+// order). A CTA takes 16 columns at a time: one thread per (token, pair,
+// column) loads and sums that pair's shares into shared memory, then one
+// thread per (token, column) folds the pairs in order.
+constexpr int kCombCols = 16;
+ES_DEV void small_combine(const SmallArgs& a, const SmallState& st, float* ys) {
+  const int RQ = a.D / 64, KS = a.ks_dn, T = a.T;
+  constexpr int S = kMaxTopK + 1;
+  const int n_tiles = a.D / kCombCols;
+  for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    const int d0 = tile * kCombCols;
+    for (int w = threadIdx.x; w < T * S * kCombCols; w += kSmThreads) {
+      const int dc = w % kCombCols, ts = w / kCombCols, t = ts / S, s = ts - t * S;
+      if (s >= st.tok_n[t]) continue;
+      const int p = st.tok_pair[t * S + s];
+      const int d = d0 + dc, rq = d >> 6, j = (d >> 4) & 3, r = d & 15;
+      const int u = st.pair_u[p], col = p - st.act_off[u];
+      const float* src = a.part + (size_t)(u * RQ + rq) * KS * 512 +
+                         ((r & 7) * 4 + (col >> 1)) * 16 + j * 4 + (r >= 8 ? 2 : 0) + (col & 1);
+      float part[kMaxSplitK];
+#pragma unroll
+      for (int ks = 0; ks < kMaxSplitK; ++ks) part[ks] = ks < KS ? __ldcg(src + (size_t)ks * 512) : 0.f;
+      float y = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < kMaxSplitK; ++ks) y += part[ks];
+      ys[w] = y;
+    }
+    __syncthreads();
+    for (int w = threadIdx.x; w < T * kCombCols; w += kSmThreads) {
+      const int t = w / kCombCols, dc = w % kCombCols;
+      float acc = 0.f;
+      for (int s = 0; s < st.tok_n[t]; ++s)
+        acc = fmaf(st.pair_w[st.tok_pair[t * S + s]], ys[(t * S + s) * kCombCols + dc], acc);
+      const size_t i = (size_t)t * a.D + d0 + dc;
+      if (a.out_f32) static_cast<float*>(a.out)[i] = acc;
+      else static_cast<uint16_t*>(a.out)[i] = float_to_bf16_bits(acc);
+    }
+    __syncthreads();
+  }
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(kSmThreads, 1) small_block_kernel(SmallArgs a) {
+  extern __shared__ __align__(16) uint8_t sm_dyn[];
+  __shared__ SmallState st;
+  __shared__ float ys[kSmMaxT * (kMaxTopK + 1) * kCombCols];
+  uint16_t* xs = reinterpret_cast<uint16_t*>(sm_dyn);
+  float* xsum = reinterpret_cast<float*>(sm_dyn + (size_t)a.T * a.D * 2);
+  const int warp = threadIdx.x >> 5;
+  // items go round the CTAs first, so a phase with fewer items than warps
+  // still spreads its loads over every SM
+  const int gw = warp * gridDim.x + blockIdx.x, nw = gridDim.x * kSmWarps;
+  small_route<VPL>(a, st);
+  small_stage_x(a, xs, xsum);
+  const int RP = a.I / 32, RQ = a.D / 64;
+  // phase 1: gate/up partials
+  {
+    const int items = st.n_act * RP * a.ks_gu;
+    for (int it = gw; it < items; it += nw) {
+      const int ks = it % a.ks_gu, rest = it / a.ks_gu;
+      small_gateup_item(a, st, xs, xsum, rest / RP, rest % RP, ks);
+    }
+  }
+  grid_barrier(a.bar, 1, a.err);
+  // phase 2: reduce + SwiGLU -> h
+  for (int it = gw; it < st.n_act * RP; it += nw) small_reduce_item(a, st, it / RP, it % RP);
+  grid_barrier(a.bar, 2, a.err);
+  // phase 3: down partials
+  {
+    const int items = st.n_act * RQ * a.ks_dn;
+    for (int it = gw; it < items; it += nw) {
+      const int ks = it % a.ks_dn, rest = it / a.ks_dn;
+      small_down_item(a, st, rest / RQ, rest % RQ, ks);
+    }
+  }
+  grid_barrier(a.bar, 3, a.err);
+  small_combine(a, st, ys);
+  // the last CTA out returns both counters to zero for the next call
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (atomicAdd(a.bar + 1, 1u) == gridDim.x - 1) {
+      a.bar[0] = 0u;
+      a.bar[1] = 0u;
+    }
+  }
+}
+
+// largest divisor of n that is <= cap
+int share_count(int n, int cap) {
+  for (int s = cap; s > 1; --s)
+    if (n % s == 0) return s;
+  return 1;
+}
+
+template <int VPL>
+cudaError_t launch_small_vpl(SmallArgs a, cudaStream_t st) {
+  const size_t smem = (size_t)a.T * a.D * 2 + (size_t)a.T * (a.D / kGroup) * 4;
+  cudaError_t e = cudaFuncSetAttribute(small_block_kernel<VPL>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, small_block_kernel<VPL>, kSmThreads,
+                                                    smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sm_count());
+  cfg.blockDim = dim3(kSmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: grid barriers are safe
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, small_block_kernel<VPL>, a);
+}
+
+}  // namespace
+
+bool small_path_fits(int T, int D, int I, int E, int k, int has_shared) {
+  (void)E;
+  (void)has_shared;
+  return T >= 1 && T <= kSmallMaxTokens && D % 64 == 0 && D <= 4096 && I % 64 == 0 &&
+         (I / 32) >= 1 && T * k <= kSmThreads;
+}
+
+cudaError_t launch_small(SmallArgs a, cudaStream_t st) {
+  a.ks_gu = share_count(a.D / kGroup, kMaxSplitK);
+  a.ks_dn = share_count(a.I / kGroup, kMaxSplitK);
+  const int vpl = (a.E + 31) / 32;
+  if (vpl <= 1) return launch_small_vpl<1>(a, st);
+  if (vpl <= 2) return launch_small_vpl<2>(a, st);
+  if (vpl <= 4) return launch_small_vpl<4>(a, st);
+  if (vpl <= 8) return launch_small_vpl<8>(a, st);
+  if (vpl <= 16) return launch_small_vpl<16>(a, st);
+  return launch_small_vpl<32>(a, st);
+}
+
+}  // namespace es

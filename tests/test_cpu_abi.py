@@ -66,7 +66,7 @@ def test_workspace_bytes_monotone(lib):
 @pytest.mark.parametrize("bad", [
     dict(group_size=32), dict(bits=8), dict(hidden=2000), dict(hidden=8192), dict(inter=640),
     dict(num_experts=2000), dict(top_k=17), dict(top_k=0), dict(shared_inter=256),
-    dict(kernel_path=4), dict(kernel_path=-1),
+    dict(kernel_path=5), dict(kernel_path=-1),
 ])
 def test_unsupported_configs_rejected(lib, bad):
     base = dict(hidden=2048, num_experts=128, top_k=8, inter=768, group_size=64, bits=4,
@@ -123,14 +123,16 @@ def test_config_validation_in_python():
 
 def test_automatic_kernel_choice():
     """The automatic expert-FFN kernel rule (es_moe_cfg.kernel_path 0), by
-    average pairs per routed expert p = T k / E: decode below 4, 32-token
-    tensor tiles up to 48, 128-token tiles above; tensor kernels from T = 64;
-    fp16 activations never take the decode kernels."""
+    average pairs per routed expert p = T k / E: the fused tiny-batch kernel
+    for T <= 4, decode below 4, 32-token tensor tiles up to 48, 128-token
+    tiles above; tensor kernels from T = 64; fp16 activations never take the
+    decode or fused kernels."""
     from expert_sniper_b200.block import ffn_kernels, uses_tensor_path
     q = PRESETS["qwen3-30b-a3b"]          # E = 128, k = 8
-    assert [ffn_kernels(q, T) for T in (1, 8, 63, 64, 128, 256, 768, 769, 4096)] == [
-        "decode", "decode", "decode", "tensor-small", "tensor-small", "tensor-small",
-        "tensor-small", "tensor", "tensor"]
+    assert [ffn_kernels(q, T) for T in (1, 4, 5, 8, 63, 64, 128, 256, 768, 769, 4096)] == [
+        "fused", "fused", "decode", "decode", "decode", "tensor-small", "tensor-small",
+        "tensor-small", "tensor-small", "tensor", "tensor"]
+    assert ffn_kernels(q.with_(kernel_path="fused"), 8) == "decode"
     small = MoEConfig(256, 4, 2, 256, True)  # p = T / 2: the T >= 64 floor decides
     assert ffn_kernels(small, 32) == "decode" and ffn_kernels(small, 64) == "tensor-small"
     assert ffn_kernels(small, 98) == "tensor"

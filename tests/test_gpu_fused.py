@@ -1,0 +1,117 @@
+"""The fused tiny-batch kernel (es_small.cu, kernel_path "fused", the
+automatic choice for T <= 4) against the CPU oracle, through the C ABI:
+routing as in test_gpu_block.py, outputs within 3e-3 x RMS (the decode
+kernels' arithmetic: exact 4-bit weights, fp16 h), bitwise-repeatable calls,
+given routing with masked / duplicate / out-of-range ids, the shared expert,
+every reference shape, and replay inside a CUDA graph."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from expert_sniper_b200 import MoEBlock, MoEConfig, PRESETS, _native
+from expert_sniper_b200.block import ffn_kernels
+from expert_sniper_b200.quant import cache_bias_vector, synthetic_inputs, synthetic_layer
+from oracle import c_oracle as co
+from oracle import moe_oracle as mo
+from tests._helpers import (assert_bf16_close, assert_close_rms, layer_to_numpy,
+                            oracle_weights_for)
+
+pytestmark = pytest.mark.gpu
+
+FUSED_REL = 3e-3
+SMALL = MoEConfig(256, 16, 4, 256, True, name="small")
+SHARED = MoEConfig(512, 32, 6, 512, True, shared_inter=512, name="small-shared")
+
+
+def _check(cfg, T, bias, seed, dev):
+    lay = synthetic_layer(cfg, seed=100 + seed, device=dev)
+    x, _, logits, sg = synthetic_inputs(cfg, T, seed=seed, device=dev)
+    cb = cache_bias_vector(cfg.num_experts, 0.5, seed)[0].to(dev) if bias else None
+    blk = MoEBlock(cfg.with_(kernel_path="fused"), weights=lay, shared_gate_w=sg, max_tokens=T)
+    assert ffn_kernels(blk.cfg, T) == "fused"
+    out32, idx, w = blk.forward(x, logits, cb, out_dtype=torch.float32, return_routing=True)
+    again = blk.forward(x, logits, cb, out_dtype=torch.float32)
+    out16 = blk.forward(x, logits, cb)
+    torch.cuda.synchronize()
+    assert blk.read_device_error() == 0
+    assert torch.equal(out32, again)
+    lg = logits.float().cpu().numpy()
+    cbn = None if cb is None else cb.cpu().numpy()
+    idx_n = idx.cpu().numpy()
+    ok, _, _, bad = mo.topk_parity(idx_n, lg, cbn, cfg.top_k)
+    assert ok, bad
+    w_ref = oracle_weights_for(idx_n, lg, cbn, cfg.norm_topk_prob)
+    assert np.abs(w.cpu().numpy() - w_ref).max() <= 1e-5
+    ref = co.expert_ffn(x.float().cpu().numpy(), layer_to_numpy(lay), idx_n, w_ref,
+                        None if sg is None else sg.float().cpu().numpy())
+    err, rms = assert_close_rms(out32.cpu().numpy(), ref, rel=FUSED_REL, what=f"{cfg.name} T={T}")
+    assert_bf16_close(out16.float().cpu().numpy(), ref)
+    return blk, x, logits, cb
+
+
+@pytest.mark.parametrize("T", [1, 2, 3, 4])
+@pytest.mark.parametrize("bias", [False, True])
+def test_fused_small(cuda, T, bias):
+    _check(SMALL, T, bias, seed=T, dev=cuda)
+
+
+@pytest.mark.parametrize("T", [1, 4])
+def test_fused_shared_expert(cuda, T):
+    _check(SHARED, T, True, seed=10 + T, dev=cuda)
+
+
+@pytest.mark.parametrize("name,T", [("olmoe-1b-7b", 2), ("qwen3-30b-a3b", 1),
+                                    ("qwen3-30b-a3b", 4), ("qwen3-next-80b-a3b", 3),
+                                    ("qwen3-235b-a22b", 4)])
+def test_fused_reference_shapes(cuda, name, T):
+    _check(PRESETS[name], T, name == "qwen3-30b-a3b", seed=20 + T, dev=cuda)
+
+
+def test_fused_given_routing_masked_duplicate_out_of_range(cuda):
+    cfg = SMALL.with_(kernel_path="fused")
+    lay = synthetic_layer(cfg, seed=7, device=cuda)
+    T = 4
+    x, _, _, _ = synthetic_inputs(cfg, T, seed=11, device=cuda)
+    g = np.random.default_rng(3)
+    idx = np.stack([g.choice(cfg.num_experts, cfg.top_k, replace=False) for _ in range(T)]).astype(np.int32)
+    idx[0, :] = -1                     # a token with nothing routed
+    idx[1, 1] = -1
+    idx[2, 2] = idx[2, 0]              # duplicate expert in one token
+    idx[3, 3] = cfg.num_experts + 3    # out of range: flagged, skipped
+    w = g.random((T, cfg.top_k)).astype(np.float32)
+    blk = MoEBlock(cfg, weights=lay, max_tokens=T)
+    out = blk.expert_ffn(x, torch.from_numpy(idx).to(cuda), torch.from_numpy(w).to(cuda),
+                         out_dtype=torch.float32)
+    assert blk.read_device_error() & _native.DEVERR_BAD_EXPERT_ID
+    masked = idx.copy()
+    masked[3, 3] = -1
+    ref = mo.expert_ffn(x.float().cpu().numpy(), layer_to_numpy(lay), masked, w)
+    assert_close_rms(out.cpu().numpy(), ref, rel=FUSED_REL, what="given routing")
+    assert torch.count_nonzero(out[0]) == 0
+
+
+def test_fused_in_cuda_graph(cuda):
+    blk, x, logits, cb = _check(PRESETS["qwen3-30b-a3b"], 1, True, seed=40, dev=cuda)
+    xs, ls = x.clone(), logits.clone()
+    out = torch.empty((1, blk.cfg.hidden), dtype=torch.float32, device=cuda)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        blk.forward(xs, ls, cb, out=out)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            blk.forward(xs, ls, cb, out=out)
+    torch.cuda.synchronize()
+    for seed in (41, 42, 41):
+        x2, _, l2, _ = synthetic_inputs(blk.cfg, 1, seed=seed, device=cuda)
+        xs.copy_(x2)
+        ls.copy_(l2)
+        g.replay()
+        torch.cuda.synchronize()
+        want = blk.forward(x2, l2, cb, out_dtype=torch.float32)
+        assert torch.equal(out, want)
+    assert blk.read_device_error() == 0
+    del g
