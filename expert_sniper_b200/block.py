@@ -87,14 +87,18 @@ def uses_tensor_path(cfg: MoEConfig, T: int) -> bool:
     return ffn_kernels(cfg, T) != "decode"
 
 
+# most tokens the fused tiny-batch kernel takes (kSmallMaxTokens, es_kernels.cuh)
+SMALL_MAX_TOKENS = 8
+
+
 def ffn_kernels(cfg: MoEConfig, T: int) -> str:
     """The expert-FFN kernels a call with T tokens runs ("fused", "decode",
     "tensor" or "tensor-small"): the rule of es_moe_cfg.kernel_path in
-    include/es_moe.h (automatic: the fused tiny-batch kernel for T <= 4;
+    include/es_moe.h (automatic: the fused tiny-batch kernel for T <= 8;
     otherwise by the average pairs per routed expert p = T k / E, decode
     below 4, 32-token tiles up to 48, 128-token tiles above, tensor-core
     kernels only from T = 64)."""
-    fused_fits = (cfg.x_dtype == "bf16" and 1 <= T <= 4 and cfg.hidden <= 4096
+    fused_fits = (cfg.x_dtype == "bf16" and 1 <= T <= SMALL_MAX_TOKENS and cfg.hidden <= 4096
                   and T * cfg.top_k <= 512)
     if cfg.kernel_path == "fused":
         return "fused" if fused_fits else "decode"

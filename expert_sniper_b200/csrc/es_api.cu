@@ -55,7 +55,7 @@ int ffn_variant(const es_moe_cfg* c, int T) {
   if (T >= 64 && pk >= 4LL * c->num_experts) return kFfnTensorSmall;
   // fp16 activations are read by the tensor-core kernels only
   if (c->x_dtype == ES_DTYPE_F16) return kFfnTensorSmall;
-  return (T <= es::kSmallMaxTokens && fused_fits) ? kFfnFused : kFfnDecode;
+  return fused_fits ? kFfnFused : kFfnDecode;
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -201,8 +201,8 @@ es_status run_small(const es_moe_cfg* cfg, const Workspace& w, const es::RouteAr
   a.renorm = r.renorm; a.has_shared = r.has_shared;
   a.out = out; a.out_f32 = out_f32; a.out_idx = r.out_idx; a.out_w = r.out_w;
   a.part = w.partials; a.h16 = w.h16;
-  // the split-K arrival counters are zero between calls on every path
-  a.bar = reinterpret_cast<unsigned*>(w.counters); a.err = w.err;
+  // the counter region is zero between calls on every path
+  a.ctr = w.counters; a.err = w.err;
   if (mk.mark(0, st) != cudaSuccess) return ES_ERR_CUDA;
   if (es::launch_small(a, st) != cudaSuccess) return ES_ERR_CUDA;
   for (int i = 1; i <= 5; ++i)

@@ -132,7 +132,7 @@ struct alignas(64) PfArgs {
   uint32_t* err;
 };
 
-// The fused tiny-batch block (es_small.cu), T <= 4.
+// The fused tiny-batch block (es_small.cu), T <= kSmallMaxTokens.
 struct SmallArgs {
   // routing source: logits (+ optional bias) or given top-k
   const void* logits;
@@ -152,7 +152,7 @@ struct SmallArgs {
   float* out_w;
   float* part;              // split-K partial sums (gate/up, then reused by down)
   uint16_t* h16;            // [P][I] fp16, fragment order
-  unsigned* bar;            // [2] grid-barrier counters, zero between calls
+  int* ctr;                 // [2] grid-barrier counters, zero between calls
   uint32_t* err;
 };
 
@@ -211,8 +211,9 @@ cudaError_t launch_pf_gateup(const PfArgs& a, long long tokens, int max_units, b
 cudaError_t launch_pf_down(const PfArgs& a, long long pairs, int max_units, bool small,
                            cudaStream_t st);
 cudaError_t launch_prepare(const PrepareArgs& a, cudaStream_t st);
-// fused tiny-batch block: whether a call can take it, and the launch
-constexpr int kSmallMaxTokens = 4;
+// fused tiny-batch block: whether a call can take it (T <= kSmallMaxTokens,
+// also the automatic choice's limit), and the launch
+constexpr int kSmallMaxTokens = 8;
 bool small_path_fits(int T, int D, int I, int E, int k, int has_shared);
 cudaError_t launch_small(SmallArgs a, cudaStream_t st);
 

@@ -134,6 +134,17 @@ inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
   };
   size_t o_err = take(256);
   size_t o_ctl = take(256);
+  // The regions that must be zero when a call starts sit first, at offsets
+  // that do not depend on T, so that calls with different T on one
+  // workspace find them zero: the counters (the split-K arrivals of the
+  // decode kernels, used up to kSplitKMaxTokens tokens, and the fused
+  // tiny-batch kernel's two barrier words), sized for kSplitKMaxTokens
+  // tokens whatever T is; then the token bitmaps, whose size grows with T
+  // (a smaller T uses a prefix of the region).
+  const size_t As8 = (size_t)(((long long)kSplitKMaxTokens * k < E ? kSplitKMaxTokens * k : E) +
+                              (has_shared ? 1 : 0));
+  const size_t cnt_all = As8 * (I / 32) > As8 * (D / 64) ? As8 * (I / 32) : As8 * (D / 64);
+  size_t o_cnt = take(cnt_all * 4);
   size_t o_bitmap = take((size_t)E1 * W * 4);
   size_t o_wpre = take((size_t)E1 * W * 4);
   size_t o_nact = take(4);
@@ -152,8 +163,6 @@ inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
   size_t o_xs = take((size_t)Tm * (D / kGroup) * 4);
   size_t o_hh = take((size_t)P * I * 2);
   size_t o_y = take((size_t)P * D * 4);
-  const long long routed = (long long)Tm * k < E ? (long long)Tm * k : E;
-  const size_t A = (size_t)routed + (has_shared ? 1 : 0);  // most active experts
   // split-K partials are used up to kSplitKMaxTokens tokens; larger T keeps
   // that amount so the size never shrinks as T grows
   const long long Ts = Tm < kSplitKMaxTokens ? Tm : kSplitKMaxTokens;
@@ -163,12 +172,10 @@ inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
   const size_t dn_slots = As * (D / 64) * kMaxSplitK;
   const size_t part_items = gu_slots > dn_slots ? gu_slots : dn_slots;
   size_t o_part = take(part_items * 512 * 4);
-  const size_t cnt_gu = A * (I / 32), cnt_dn = A * (D / 64);
-  size_t o_cnt = take((cnt_gu > cnt_dn ? cnt_gu : cnt_dn) * 4);
   w.bytes = off;
-  w.zero_ctl_bytes = o_bitmap - o_err;
+  w.zero_ctl_bytes = o_cnt - o_err;
   w.zero_bitmap_bytes = (size_t)E1 * W * 4;
-  w.zero_counter_bytes = (cnt_gu > cnt_dn ? cnt_gu : cnt_dn) * 4;
+  w.zero_counter_bytes = cnt_all * 4;
   w.W = W;
   w.P = P;
   w.kk = kk;

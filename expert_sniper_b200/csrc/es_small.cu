@@ -1,4 +1,4 @@
-// The whole MoE block for tiny batches (T <= 4 tokens) in one cooperative
+// The whole MoE block for tiny batches (T <= 8 tokens) in one cooperative
 // kernel: router, gate/up + SwiGLU, down and combine, with three grid-wide
 // barriers between the phases instead of four dependent launches.
 //
@@ -9,11 +9,12 @@
 // weight is the sigmoid gate).
 //
 // Phases (grid = one CTA per SM, all co-resident: cooperative launch):
-//   0  every CTA: route the T tokens (warp per token), list the distinct
-//      experts in ascending id with their (token, weight) pairs, and stage x
-//      in fragment order with 64-group sums in shared memory
-//   1  gate/up: items (expert, 32-row pair of I, K share) spread over all
-//      warps; codes stream from HBM straight into registers (two groups in
+//   0  every CTA: route the T tokens (warp per token) while the other warps
+//      stage x in fragment order with 64-group sums in shared memory, then
+//      list the distinct experts in ascending id with their (token, weight)
+//      pairs
+//   1  gate/up: items (expert, 32-row pair of I, K share) dealt round the
+//      CTAs; codes stream from HBM straight into registers (two groups in
 //      flight), one m16n8k16 MMA step per 16 K on the exact 128 + q codes,
 //      scale and bias applied per (row, group) in fp32: w = s q + b with no
 //      weight rounding; each item writes its fp32 partial sums
@@ -26,7 +27,7 @@
 //   -- barrier --
 //   4  combine: each output element sums its token's slots in ascending
 //      expert id (the K shares of each in fixed order), then the shared
-//      expert; bf16 or fp32 out
+//      expert; bf16 or fp32 out, 16-column tiles per CTA
 // All arithmetic is fixed-order, so results are bitwise repeatable. Every
 // barrier wait is bounded (about a second) and reports ES_DEVERR_TIMEOUT.
 #include <cooperative_groups.h>
@@ -40,7 +41,9 @@ namespace {
 
 constexpr int kSmWarps = 16;
 constexpr int kSmThreads = kSmWarps * 32;
-constexpr int kSmMaxT = 4;
+constexpr int kSmMaxT = kSmallMaxTokens;
+static_assert(kSmMaxT < kSmWarps, "routing warps and staging warps are disjoint");
+static_assert(kSmMaxT <= kSplitKMaxTokens, "partials and counters are sized up to kSplitKMaxTokens");
 constexpr int kSmMaxPairs = kSmMaxT * kMaxTopK + kSmMaxT;  // routed + shared
 constexpr uint32_t kErrTimeout = 0x8u;
 constexpr uint32_t kErrRange = 0x10u;
@@ -84,10 +87,29 @@ struct SmallState {
   float sgate[kSmMaxT];
 };
 
-// Phase 0: route the T tokens (warp t routes token t) or read the given
-// routing, and list the pairs in (expert id, token, slot) order.
+// x rows -> shared memory in fragment order, with 64-group sums, by the
+// threads from tid0 up (whole warps); no barrier of its own
+ES_DEV void small_stage_x(const SmallArgs& a, uint16_t* xs, float* xsum, int tid0) {
+  const unsigned full = 0xffffffffu;
+  const int chunks = a.D / 8, GD = a.D / kGroup;
+  const int total = a.T * chunks, nthr = kSmThreads - tid0;
+  for (int c0 = 0; c0 < total; c0 += nthr) {
+    const int c = c0 + (int)threadIdx.x - tid0;
+    const bool lv = c < total;
+    const int tt = lv ? c / chunks : 0, q8 = lv ? c % chunks : 0;
+    float sum = permute_chunk8(a.x + (size_t)tt * a.D, xs + (size_t)tt * a.D, q8, lv);
+    sum += __shfl_xor_sync(full, sum, 1);
+    sum += __shfl_xor_sync(full, sum, 2);
+    sum += __shfl_xor_sync(full, sum, 4);
+    if (lv && (q8 & 7) == 0) xsum[tt * GD + (q8 >> 3)] = sum;
+  }
+}
+
+// Route: the T tokens (warp t routes token t) or read the given
+// routing while the warps from kSmMaxT up stage x, and list the pairs in
+// (expert id, token, slot) order.
 template <int VPL>
-ES_DEV void small_route(const SmallArgs& a, SmallState& st) {
+ES_DEV void small_route(const SmallArgs& a, SmallState& st, uint16_t* xs, float* xsum) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int k = a.k, T = a.T;
   if (warp < T) {
@@ -117,11 +139,15 @@ ES_DEV void small_route(const SmallArgs& a, SmallState& st) {
       const float gs = shared_gate_warp(a.x + (size_t)t * a.D, a.sg_w, a.D);
       if (lane == 0) st.sgate[t] = gs;
     }
+  } else if (warp >= kSmMaxT) {
+    small_stage_x(a, xs, xsum, kSmMaxT * 32);
   }
   __syncthreads();
   // one thread per slot: whether it is the first slot of its expert, then
   // its rank among the valid slots by (expert, slot index) -- its pair
-  // index -- and, for a first slot, the expert's entry
+  // index -- and, for a first slot, the expert's entry; and its place in
+  // its token's own pair list (ascending expert id)
+  constexpr int S = kMaxTopK + 1;
   const int ns = T * k;
   const int s = threadIdx.x;
   const bool valid = s < ns && st.slot_e[s] >= 0;
@@ -133,69 +159,59 @@ ES_DEV void small_route(const SmallArgs& a, SmallState& st) {
   const int n_routed = __syncthreads_count(valid);
   const int n_first = __syncthreads_count(first);
   if (valid) {
-    const int e = st.slot_e[s];
+    const int e = st.slot_e[s], t = s / k;
     int rank = 0, first_rank = 0, cnt_same = 0;
+#pragma unroll 8
     for (int s2 = 0; s2 < ns; ++s2) {
       const int e2 = st.slot_e[s2];
-      if (e2 < 0) continue;
-      rank += (e2 < e || (e2 == e && s2 < s)) ? 1 : 0;
+      const bool v2 = e2 >= 0;
+      rank += (v2 && (e2 < e || (e2 == e && s2 < s))) ? 1 : 0;
       cnt_same += e2 == e;
-      first_rank += (e2 < e && st.first[s2]) ? 1 : 0;
+      first_rank += (v2 && e2 < e && st.first[s2]) ? 1 : 0;
     }
-    st.pair_tok[rank] = s / k;
+    int tpos = 0;
+    for (int j = 0; j < k; ++j) {
+      const int s2 = t * k + j, e2 = st.slot_e[s2];
+      tpos += (e2 >= 0 && (e2 < e || (e2 == e && s2 < s))) ? 1 : 0;
+    }
+    st.pair_tok[rank] = t;
     st.pair_w[rank] = st.slot_w[s];
     st.pair_u[rank] = first_rank;
+    st.tok_pair[t * S + tpos] = rank;
     if (first) {
       st.act_e[first_rank] = e;
       st.act_off[first_rank] = rank;
       st.act_n[first_rank] = cnt_same;
     }
   }
-  if (threadIdx.x == 0) {
-    int n_act = n_first, n_pairs = n_routed;
+  // one thread per token: its pair count, and its shared-expert pair (the
+  // last entry, after every routed expert)
+  if (s < T) {
+    int nv = 0;
+    for (int j = 0; j < k; ++j) nv += st.slot_e[s * k + j] >= 0 ? 1 : 0;
     if (a.has_shared) {
-      st.act_e[n_act] = a.E;
-      st.act_off[n_act] = n_pairs;
-      st.act_n[n_act] = T;
-      for (int t = 0; t < T; ++t) {
-        st.pair_tok[n_pairs + t] = t;
-        st.pair_w[n_pairs + t] = st.sgate[t];
-        st.pair_u[n_pairs + t] = n_act;
-      }
-      ++n_act;
-      n_pairs += T;
+      const int p = n_routed + s;
+      st.pair_tok[p] = s;
+      st.pair_w[p] = st.sgate[s];
+      st.pair_u[p] = n_first;
+      st.tok_pair[s * S + nv] = p;
+      ++nv;
     }
-    st.n_act = n_act;
-    st.n_pairs = n_pairs;
-    // each token's pairs in ascending pair index = ascending expert id
-    for (int t = 0; t < T; ++t) st.tok_n[t] = 0;
-    for (int p = 0; p < n_pairs; ++p) {
-      const int t = st.pair_tok[p];
-      st.tok_pair[t * (kMaxTopK + 1) + st.tok_n[t]++] = p;
+    st.tok_n[s] = nv;
+  }
+  if (s == 0) {
+    if (a.has_shared) {
+      st.act_e[n_first] = a.E;
+      st.act_off[n_first] = n_routed;
+      st.act_n[n_first] = T;
     }
+    st.n_act = n_first + (a.has_shared ? 1 : 0);
+    st.n_pairs = n_routed + (a.has_shared ? T : 0);
   }
   __syncthreads();
 }
 
-// x rows -> shared memory in fragment order, with 64-group sums
-ES_DEV void small_stage_x(const SmallArgs& a, uint16_t* xs, float* xsum) {
-  const unsigned full = 0xffffffffu;
-  const int chunks = a.D / 8, GD = a.D / kGroup;
-  const int total = a.T * chunks;
-  for (int c0 = 0; c0 < total; c0 += kSmThreads) {
-    const int c = c0 + threadIdx.x;
-    const bool lv = c < total;
-    const int tt = lv ? c / chunks : 0, q8 = lv ? c % chunks : 0;
-    float sum = permute_chunk8(a.x + (size_t)tt * a.D, xs + (size_t)tt * a.D, q8, lv);
-    sum += __shfl_xor_sync(full, sum, 1);
-    sum += __shfl_xor_sync(full, sum, 2);
-    sum += __shfl_xor_sync(full, sum, 4);
-    if (lv && (q8 & 7) == 0) xsum[tt * GD + (q8 >> 3)] = sum;
-  }
-  __syncthreads();
-}
-
-// Phase 1, one item: expert entry u, row pair rp (32 rows of I: two 16-row
+// Gate/up item: expert entry u, row pair rp (32 rows of I: two 16-row
 // blocks, gate and up), K share ks of GPI groups. Partial sums per lane:
 // [block j][gate v0..3 | up v0..3] -> part[((u * RP + rp) * KS + ks) * 512].
 ES_DEV void small_gateup_item(const SmallArgs& a, const SmallState& st, const uint16_t* xs,
@@ -272,8 +288,8 @@ ES_DEV void small_gateup_item(const SmallArgs& a, const SmallState& st, const ui
                          acc[q >> 1][(q & 1) * 4 + 2], acc[q >> 1][(q & 1) * 4 + 3]);
 }
 
-// Phase 2, one item (u, rp): the K shares summed in order, SwiGLU, h in
-// fp16 (fragment order) for the expert's pairs.
+// Reduce item (u, rp): the K shares summed in order, SwiGLU, h in fp16
+// (fragment order) for the expert's pairs.
 ES_DEV void small_reduce_item(const SmallArgs& a, const SmallState& st, int u, int rp) {
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -321,9 +337,10 @@ ES_DEV void small_reduce_item(const SmallArgs& a, const SmallState& st, int u, i
   if (range) set_error(a.err, kErrRange);
 }
 
-// Phase 3, one item: expert entry u, row quad rq (64 rows of D), I share ks
+// Down item: expert entry u, row quad rq (64 rows of D), I share ks
 // of GPI groups. fp16 codes 1024 + q against fp16 h (exact products), scale
-// and bias per (row, group) on the fp32 sums. Partial sums per lane:
+// and bias per (row, group) on the fp32 sums. The weights and h of the next
+// group are loaded while this one is multiplied. Partial sums per lane:
 // [block j][v] -> part[((u * RQ + rq) * KS + ks) * 512].
 ES_DEV void small_down_item(const SmallArgs& a, const SmallState& st, int u, int rq, int ks) {
   const unsigned full = 0xffffffffu;
@@ -332,6 +349,8 @@ ES_DEV void small_down_item(const SmallArgs& a, const SmallState& st, int u, int
   const int GI = a.I / kGroup, RQ = a.D / 64, KS = a.ks_dn, GPI = GI / KS;
   const int e = st.act_e[u], p0 = st.act_off[u], n = st.act_n[u];
   const uint8_t* base = a.packed + (size_t)e * a.expert_bytes;
+  const uint4* hrow = g < n ? reinterpret_cast<const uint4*>(a.h16 + (size_t)(p0 + g) * a.I + c * 16)
+                            : nullptr;
   float acc[4][4];
 #pragma unroll
   for (int j = 0; j < 4; ++j)
@@ -339,7 +358,8 @@ ES_DEV void small_down_item(const SmallArgs& a, const SmallState& st, int u, int
     for (int v = 0; v < 4; ++v) acc[j][v] = 0.f;
   uint4 cw[2][4];
   uint2 sb[2][4];
-  auto load = [&](int G, uint4 (&w)[4], uint2 (&b)[4]) {
+  uint4 hv[2][2];
+  auto load_w = [&](int G, uint4 (&w)[4], uint2 (&b)[4]) {
     const uint8_t* run = base + down_tile_off(a.D, a.I, 4 * rq, G);
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
@@ -347,22 +367,28 @@ ES_DEV void small_down_item(const SmallArgs& a, const SmallState& st, int u, int
       b[t] = __ldg(reinterpret_cast<const uint2*>(run + t * kTileBytes + kTileCodeBytes + g * 8));
     }
   };
+  auto load_h = [&](int G, uint4 (&h)[2]) {
+    if (hrow) {
+      h[0] = __ldcg(hrow + G * (kGroup / 8));
+      h[1] = __ldcg(hrow + G * (kGroup / 8) + 1);
+    } else {
+      h[0] = make_uint4(0, 0, 0, 0);
+      h[1] = h[0];
+    }
+  };
   const int G0 = ks * GPI;
-  load(G0, cw[0], sb[0]);
+  load_w(G0, cw[0], sb[0]);
+  load_h(G0, hv[0]);
   for (int i = 0; i < GPI; ++i) {
     const int G = G0 + i, cur = i & 1;
     if (i + 1 < GPI) {
-      if (cur == 0) load(G + 1, cw[1], sb[1]);
-      else load(G + 1, cw[0], sb[0]);
+      if (cur == 0) { load_w(G + 1, cw[1], sb[1]); load_h(G + 1, hv[1]); }
+      else { load_w(G + 1, cw[0], sb[0]); load_h(G + 1, hv[0]); }
     }
     uint32_t hw[8];
     {
-      uint4 h0 = make_uint4(0, 0, 0, 0), h1 = h0;
-      if (g < n) {
-        const uint4* hp = reinterpret_cast<const uint4*>(a.h16 + (size_t)(p0 + g) * a.I + G * kGroup + c * 16);
-        h0 = __ldcg(hp);
-        h1 = __ldcg(hp + 1);
-      }
+      const uint4 h0 = cur == 0 ? hv[0][0] : hv[1][0];
+      const uint4 h1 = cur == 0 ? hv[0][1] : hv[1][1];
       hw[0] = h0.x; hw[1] = h0.y; hw[2] = h0.z; hw[3] = h0.w;
       hw[4] = h1.x; hw[5] = h1.y; hw[6] = h1.z; hw[7] = h1.w;
     }
@@ -396,7 +422,7 @@ ES_DEV void small_down_item(const SmallArgs& a, const SmallState& st, int u, int
   for (int j = 0; j < 4; ++j) out[j] = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
 }
 
-// Phase 4: out[t][d] = sum over the token's pairs (ascending expert id, the
+// Combine: out[t][d] = sum over the token's pairs (ascending expert id, the
 // shared expert last) of weight x (its down partials summed in share
 // order). A CTA takes 16 columns at a time: one thread per (token, pair,
 // column) loads and sums that pair's shares into shared memory, then one
@@ -445,12 +471,12 @@ __global__ void __launch_bounds__(kSmThreads, 1) small_block_kernel(SmallArgs a)
   __shared__ float ys[kSmMaxT * (kMaxTopK + 1) * kCombCols];
   uint16_t* xs = reinterpret_cast<uint16_t*>(sm_dyn);
   float* xsum = reinterpret_cast<float*>(sm_dyn + (size_t)a.T * a.D * 2);
+  unsigned* bar = reinterpret_cast<unsigned*>(a.ctr);
   const int warp = threadIdx.x >> 5;
   // items go round the CTAs first, so a phase with fewer items than warps
   // still spreads its loads over every SM
   const int gw = warp * gridDim.x + blockIdx.x, nw = gridDim.x * kSmWarps;
-  small_route<VPL>(a, st);
-  small_stage_x(a, xs, xsum);
+  small_route<VPL>(a, st, xs, xsum);
   const int RP = a.I / 32, RQ = a.D / 64;
   // phase 1: gate/up partials
   {
@@ -460,10 +486,10 @@ __global__ void __launch_bounds__(kSmThreads, 1) small_block_kernel(SmallArgs a)
       small_gateup_item(a, st, xs, xsum, rest / RP, rest % RP, ks);
     }
   }
-  grid_barrier(a.bar, 1, a.err);
+  grid_barrier(bar, 1, a.err);
   // phase 2: reduce + SwiGLU -> h
   for (int it = gw; it < st.n_act * RP; it += nw) small_reduce_item(a, st, it / RP, it % RP);
-  grid_barrier(a.bar, 2, a.err);
+  grid_barrier(bar, 2, a.err);
   // phase 3: down partials
   {
     const int items = st.n_act * RQ * a.ks_dn;
@@ -472,14 +498,14 @@ __global__ void __launch_bounds__(kSmThreads, 1) small_block_kernel(SmallArgs a)
       small_down_item(a, st, rest / RQ, rest % RQ, ks);
     }
   }
-  grid_barrier(a.bar, 3, a.err);
+  grid_barrier(bar, 3, a.err);
   small_combine(a, st, ys);
   // the last CTA out returns both counters to zero for the next call
   __syncthreads();
   if (threadIdx.x == 0) {
-    if (atomicAdd(a.bar + 1, 1u) == gridDim.x - 1) {
-      a.bar[0] = 0u;
-      a.bar[1] = 0u;
+    if (atomicAdd(bar + 1, 1u) == gridDim.x - 1) {
+      bar[0] = 0u;
+      bar[1] = 0u;
     }
   }
 }
