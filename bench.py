@@ -648,11 +648,20 @@ def run_ours_ep(args):
     torch.cuda.set_device(dev)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    cfg = PRESETS[args.model]
-    T, L = args.tokens, max(2, args.layers)
+    # --workload prefill: the Qwen3-Next layer over --prefill-tokens prompt
+    # tokens split across the GPUs (strong scaling), no routing bias, two
+    # alternating layers, as the one-GPU prefill line
+    prefill = args.workload == "prefill"
+    cfg = PRESETS["qwen3-next-80b-a3b" if prefill else args.model]
+    if prefill:
+        if args.prefill_tokens % world:
+            raise SystemExit("--prefill-tokens must divide by the number of GPUs")
+        T, L = args.prefill_tokens // world, 2
+    else:
+        T, L = args.tokens, max(2, args.layers)
     pl = ep.make_placement(cfg.num_experts, world, args.placement)
     lcfg = cfg.with_(num_experts=max(1, max(pl.counts)))
-    bias = cache_bias_vector(cfg.num_experts, 0.5, 0)[0].to(dev)
+    bias = None if prefill else cache_bias_vector(cfg.num_experts, 0.5, 0)[0].to(dev)
     p2p = args.ep_mode == "p2p"
     wins = ep.EpWindows(world, rank, T, cfg.hidden, cfg.top_k, dev) if p2p else None
     ws = MoEBlock.new_workspace(lcfg, world * T, dev)
@@ -660,14 +669,16 @@ def run_ours_ep(args):
     t_setup = time.time()
     for l in range(L):
         lay = synthetic_layer(cfg, seed=1000 + l, device=dev)
+        x, _, lg, sg = synthetic_inputs(cfg, T, seed=100_000 * rank + l, device=dev)
+        if sg is not None:   # one shared-gate vector per layer on every rank
+            sg = synthetic_inputs(cfg, 1, seed=1000 + l, device=dev)[3]
         if p2p:
-            backends.append(ep.P2PEPBackend(cfg, pl, rank, wins, layer=lay,
+            backends.append(ep.P2PEPBackend(cfg, pl, rank, wins, layer=lay, shared_gate_w=sg,
                                             local_workspace=ws))
         else:
             backends.append(ep.CudaEPBackend(cfg, pl, rank, layer=lay, max_tokens=T, device=dev,
                                              workspace=ws))
         del lay
-        x, _, lg, _ = synthetic_inputs(cfg, T, seed=100_000 * rank + l, device=dev)
         xs.append(x)
         lgs.append(lg)
     torch.cuda.synchronize()
@@ -695,7 +706,7 @@ def run_ours_ep(args):
         return ep.ep_forward(b, xs[s % L], lgs[s % L], bias)
 
     W = max(3, args.warmup)
-    K = args.steps
+    K = min(args.steps, args.prefill_steps) if prefill else args.steps
     stream = torch.cuda.Stream(dev)
     stream.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(stream):
@@ -804,16 +815,26 @@ def run_ours_ep(args):
     if rank == 0:
         peak, peak_kind = measured_peaks()
         achieved = float(per_gpu_bytes.item()) / (ms * 1e-3) / 1e9
+        if prefill:
+            metric = PREFILL_METRIC[:-1] + ", expert-parallel)"
+            workload = (f"{cfg.name} MoE layer prefill, {world * T} tokens split over {world} "
+                        f"GPUs ({T} each), experts sharded ({args.placement}), no routing bias, "
+                        f"{L} alternating layers")
+        else:
+            metric = (METRIC if args.model == "qwen3-30b-a3b" else
+                      f"MoE-layer decode tokens/s ({args.model}-shaped 4-bit layer, "
+                      "expert-parallel)")
+            workload = (f"{cfg.name} MoE layer decode, {T} home tokens per GPU, experts sharded "
+                        f"over {world} GPUs ({args.placement}), routing bias +0.5, {L} rotating "
+                        "layers")
         line = {
-            "metric": METRIC if args.model == "qwen3-30b-a3b" else
-            f"MoE-layer decode tokens/s ({args.model}-shaped 4-bit layer, expert-parallel)",
+            "metric": metric,
             "value": world * T / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "u4xbf16->f32",
+            "scaling": "strong" if prefill else "weak", "vs_baseline": None,
+            "dtype": "u4xbf16->f32",
             "data": "synthetic (seeded; random-init 4-bit MLX-affine experts)",
-            "config": {"workload": f"{cfg.name} MoE layer decode, {T} home tokens per GPU, "
-                                   f"experts sharded over {world} GPUs ({args.placement}), "
-                                   f"routing bias +0.5, {L} rotating layers",
+            "config": {"workload": workload,
                        "model": cfg.name, "tokens_per_gpu": T, "global_batch": world * T,
                        "parallelism": f"ep{world}", "placement": args.placement,
                        "exchange": args.ep_mode, "experts_per_gpu": pl.counts,
@@ -830,12 +851,25 @@ def run_ours_ep(args):
             # tensor-core kernels), return, combine_p2p
             "gpu_launches": (10 if p2p else 7) * K,
             "phase_ms": phases,
+            "tflops": (2 * world * T * (cfg.top_k * 3 * cfg.hidden * cfg.inter
+                                         + 3 * cfg.hidden * cfg.shared_inter)
+                       / (ms * 1e-3) / 1e12) if prefill else None,
             "device_error": int(errs.item()),
             "clocks": clk,
             "cpu_baseline": None,
             "setup_s": setup_s,
             "note": note,
         }
+        if prefill:
+            tpeak, tkind = 1590.0, "fallback"
+            pp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+            if os.path.exists(pp):
+                with open(pp) as f:
+                    tpeak, tkind = float(json.load(f).get("bf16_tflops", 1590.0)), "measured"
+            line["roofline"] = {"bound": "tensor", "kernel": "whole step (all GPUs)",
+                                "achieved": line["tflops"] / world, "peak": tpeak,
+                                "peak_kind": tkind, "unit": "TFLOP/s per GPU",
+                                "frac": line["tflops"] / world / tpeak, "traffic": None}
         print(json.dumps(line), flush=True)
     del graphs
     torch.cuda.synchronize()

@@ -48,7 +48,12 @@ def _emulated_step(bes, xs, lgs, bias, T):
 
 @pytest.mark.parametrize("cfg,world,policy,T", [(SMALL, 1, "hrw", 5), (SMALL, 2, "hrw", 7),
                                                 (SMALL, 4, "bounded", 3),
-                                                (PRESETS["qwen3-30b-a3b"], 8, "bounded", 64)])
+                                                (PRESETS["qwen3-30b-a3b"], 8, "bounded", 64),
+                                                # prefill-sized: the owners run the 128-token
+                                                # tensor-core kernels, the full block the
+                                                # 32-token ones
+                                                (PRESETS["qwen3-next-80b-a3b"], 2, "bounded",
+                                                 1024)])
 def test_p2p_emulated_ranks(cuda, cfg, world, policy, T):
     lay = synthetic_layer(cfg, seed=3, device=cuda)
     pl = ep.make_placement(cfg.num_experts, world, policy)
