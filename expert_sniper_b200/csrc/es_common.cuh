@@ -76,6 +76,24 @@ ES_DEV uint4 ld_stream16(const void* p) {
   return r;
 }
 
+// The same 16-byte streaming load with an L2 cache policy (createpolicy),
+// e.g. evict-first for data read once per call, so that it is the first
+// to leave L2 and the small data and code around it stay.
+ES_DEV uint4 ld_stream16_pol(const void* p, uint64_t pol) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;\n"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p), "l"(pol));
+  return r;
+}
+ES_DEV uint2 ld_nc8_pol(const void* p, uint64_t pol) {
+  uint2 r;
+  asm volatile("ld.global.nc.L2::cache_hint.v2.u32 {%0,%1}, [%2], %3;\n"
+               : "=r"(r.x), "=r"(r.y)
+               : "l"(p), "l"(pol));
+  return r;
+}
+
 ES_DEV uint2 ld_stream8(const void* p) {
   uint2 r;
   asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];\n"

@@ -49,12 +49,13 @@ constexpr uint32_t kErrTimeout = 0x8u;
 constexpr uint32_t kErrRange = 0x10u;
 
 // Grid barrier b (1, 2, 3) on a counter that is zero when the kernel starts:
-// every CTA adds one and waits for b * gridDim.x arrivals (bounded).
+// every CTA adds one with a release reduction (ordering the CTA's writes,
+// collected by the block barrier, before it) and waits with acquire loads
+// for b * gridDim.x arrivals (bounded).
 ES_DEV void grid_barrier(unsigned* bar, unsigned b, uint32_t* err) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(bar, 1u);
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;\n" ::"l"(bar) : "memory");
     const unsigned target = b * gridDim.x;
     const long long t0 = clock64();
     while (true) {
@@ -221,6 +222,9 @@ ES_DEV void small_gateup_item(const SmallArgs& a, const SmallState& st, const ui
   const int GD = a.D / kGroup, RP = a.I / 32, KS = a.ks_gu, GPI = GD / KS;
   const int e = st.act_e[u], p0 = st.act_off[u], n = st.act_n[u];
   const uint8_t* base = a.packed + (size_t)e * a.expert_bytes;
+  // weights are read once per call: first out of L2, so that the kernel's
+  // code, x, the partials and h stay there
+  const uint64_t pol = l2_evict_first_policy();
   const int tb = g < n ? st.pair_tok[p0 + g] : -1;
   const int tc0 = 2 * c < n ? st.pair_tok[p0 + 2 * c] : -1;
   const int tc1 = 2 * c + 1 < n ? st.pair_tok[p0 + 2 * c + 1] : -1;
@@ -235,8 +239,8 @@ ES_DEV void small_gateup_item(const SmallArgs& a, const SmallState& st, const ui
     const uint8_t* run = base + gateup_tile_off(GD, 2 * rp, G, 0);
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-      w[t] = ld_stream16(run + t * kTileBytes + lane * 16);
-      b[t] = __ldg(reinterpret_cast<const uint2*>(run + t * kTileBytes + kTileCodeBytes + g * 8));
+      w[t] = ld_stream16_pol(run + t * kTileBytes + lane * 16, pol);
+      b[t] = ld_nc8_pol(run + t * kTileBytes + kTileCodeBytes + g * 8, pol);
     }
   };
   const int G0 = ks * GPI;
@@ -349,6 +353,9 @@ ES_DEV void small_down_item(const SmallArgs& a, const SmallState& st, int u, int
   const int GI = a.I / kGroup, RQ = a.D / 64, KS = a.ks_dn, GPI = GI / KS;
   const int e = st.act_e[u], p0 = st.act_off[u], n = st.act_n[u];
   const uint8_t* base = a.packed + (size_t)e * a.expert_bytes;
+  // weights are read once per call: first out of L2, so that the kernel's
+  // code, x, the partials and h stay there
+  const uint64_t pol = l2_evict_first_policy();
   const uint4* hrow = g < n ? reinterpret_cast<const uint4*>(a.h16 + (size_t)(p0 + g) * a.I + c * 16)
                             : nullptr;
   float acc[4][4];
@@ -363,8 +370,8 @@ ES_DEV void small_down_item(const SmallArgs& a, const SmallState& st, int u, int
     const uint8_t* run = base + down_tile_off(a.D, a.I, 4 * rq, G);
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-      w[t] = ld_stream16(run + t * kTileBytes + lane * 16);
-      b[t] = __ldg(reinterpret_cast<const uint2*>(run + t * kTileBytes + kTileCodeBytes + g * 8));
+      w[t] = ld_stream16_pol(run + t * kTileBytes + lane * 16, pol);
+      b[t] = ld_nc8_pol(run + t * kTileBytes + kTileCodeBytes + g * 8, pol);
     }
   };
   auto load_h = [&](int G, uint4 (&h)[2]) {
