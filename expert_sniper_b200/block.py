@@ -88,13 +88,13 @@ def uses_tensor_path(cfg: MoEConfig, T: int) -> bool:
 
 
 # most tokens the fused tiny-batch kernel takes (kSmallMaxTokens, es_kernels.cuh)
-SMALL_MAX_TOKENS = 8
+SMALL_MAX_TOKENS = 16
 
 
 def ffn_kernels(cfg: MoEConfig, T: int) -> str:
     """The expert-FFN kernels a call with T tokens runs ("fused", "decode",
     "tensor" or "tensor-small"): the rule of es_moe_cfg.kernel_path in
-    include/es_moe.h (automatic: the fused tiny-batch kernel for T <= 8;
+    include/es_moe.h (automatic: the fused tiny-batch kernel for T <= 16;
     otherwise by the average pairs per routed expert p = T k / E, decode
     below 4, 32-token tiles up to 48, 128-token tiles above, tensor-core
     kernels only from T = 64)."""

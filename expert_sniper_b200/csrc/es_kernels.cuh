@@ -213,7 +213,6 @@ cudaError_t launch_pf_down(const PfArgs& a, long long pairs, int max_units, bool
 cudaError_t launch_prepare(const PrepareArgs& a, cudaStream_t st);
 // fused tiny-batch block: whether a call can take it (T <= kSmallMaxTokens,
 // also the automatic choice's limit), and the launch
-constexpr int kSmallMaxTokens = 8;
 bool small_path_fits(int T, int D, int I, int E, int k, int has_shared);
 cudaError_t launch_small(SmallArgs a, cudaStream_t st);
 

@@ -49,6 +49,13 @@ constexpr int kMaxTopK = 16;
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxSplitK = 8;         // K split of gate/up items for tiny batches
 constexpr int kSplitKMaxTokens = 8;   // ... used only up to this many tokens
+// the fused one-launch kernel: most tokens, and most pairs of one expert
+// entry (an expert with more pairs takes several entries of this many)
+constexpr int kSmallMaxTokens = 16;
+constexpr int kSmallEntryPairs = 8;
+// its K split: kMaxSplitK shares up to kSplitKMaxTokens tokens, this many
+// above (twice the entries, half the shares: the same partials)
+constexpr int kSmallSplitKLarge = 4;
 
 __host__ __device__ inline size_t expert_bytes(int D, int I) {
   return (size_t)3 * D * I * 9 / 16;
@@ -163,13 +170,24 @@ inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
   size_t o_xs = take((size_t)Tm * (D / kGroup) * 4);
   size_t o_hh = take((size_t)P * I * 2);
   size_t o_y = take((size_t)P * D * 4);
-  // split-K partials are used up to kSplitKMaxTokens tokens; larger T keeps
-  // that amount so the size never shrinks as T grows
+  // split-K partials: the decode kernels use them up to kSplitKMaxTokens
+  // tokens (one entry per active expert, kMaxSplitK shares); the fused kernel
+  // the same way, and from there up to kSmallMaxTokens with entries of at
+  // most kSmallEntryPairs pairs and kSmallSplitKLarge shares. Larger T keeps
+  // the largest amount, so the size never shrinks as T grows.
   const long long Ts = Tm < kSplitKMaxTokens ? Tm : kSplitKMaxTokens;
   const size_t As = (size_t)((Ts * k < E ? Ts * k : E) + (has_shared ? 1 : 0));
+  size_t shares = As * kMaxSplitK;   // entries x shares, per row pair / quad
+  if (Tm > kSplitKMaxTokens) {
+    const long long Tf = Tm < kSmallMaxTokens ? Tm : kSmallMaxTokens;
+    const long long per_e = (Tf + kSmallEntryPairs - 1) / kSmallEntryPairs;
+    const long long routed = Tf * k < (long long)E * per_e ? Tf * k : (long long)E * per_e;
+    const size_t Af = (size_t)(routed + (has_shared ? per_e : 0));
+    if (Af * kSmallSplitKLarge > shares) shares = Af * kSmallSplitKLarge;
+  }
   // split-K slots of gate/up (row pairs) and down (row quads), 2 KB each
-  const size_t gu_slots = As * (I / 32) * kMaxSplitK;
-  const size_t dn_slots = As * (D / 64) * kMaxSplitK;
+  const size_t gu_slots = shares * (I / 32);
+  const size_t dn_slots = shares * (D / 64);
   const size_t part_items = gu_slots > dn_slots ? gu_slots : dn_slots;
   size_t o_part = take(part_items * 512 * 4);
   w.bytes = off;

@@ -1,4 +1,4 @@
-// The whole MoE block for tiny batches (T <= 8 tokens) in one cooperative
+// The whole MoE block for tiny batches (T <= 16 tokens) in one cooperative
 // kernel: router, gate/up + SwiGLU, down and combine, with three grid-wide
 // barriers between the phases instead of four dependent launches.
 //
@@ -12,7 +12,9 @@
 //   0  every CTA: route the T tokens (warp per token) while the other warps
 //      stage x in fragment order with 64-group sums in shared memory, then
 //      list the distinct experts in ascending id with their (token, weight)
-//      pairs
+//      pairs, cut into entries of at most 8 pairs (the n = 8 columns of an
+//      m16n8 MMA tile; an expert with more pairs takes several entries and
+//      streams its weights once per entry)
 //   1  gate/up: items (expert, 32-row pair of I, K share) dealt round the
 //      CTAs; codes stream from HBM straight into registers (two groups in
 //      flight), one m16n8k16 MMA step per 16 K on the exact 128 + q codes,
@@ -42,8 +44,8 @@ namespace {
 constexpr int kSmWarps = 16;
 constexpr int kSmThreads = kSmWarps * 32;
 constexpr int kSmMaxT = kSmallMaxTokens;
-static_assert(kSmMaxT < kSmWarps, "routing warps and staging warps are disjoint");
-static_assert(kSmMaxT <= kSplitKMaxTokens, "partials and counters are sized up to kSplitKMaxTokens");
+constexpr int kRouteWarps = 8;  // warps that route (token t: warp t % 8); the rest stage x
+static_assert(kRouteWarps < kSmWarps, "routing warps and staging warps are disjoint");
 constexpr int kSmMaxPairs = kSmMaxT * kMaxTopK + kSmMaxT;  // routed + shared
 constexpr uint32_t kErrTimeout = 0x8u;
 constexpr uint32_t kErrRange = 0x10u;
@@ -82,7 +84,8 @@ struct SmallState {
   int pair_u[kSmMaxPairs];     // its entry in act_*
   int slot_e[kSmMaxT * kMaxTopK];
   float slot_w[kSmMaxT * kMaxTopK];
-  int first[kSmMaxT * kMaxTopK];
+  int ent[kSmMaxT * kMaxTopK];               // at an expert's first slot: its entries
+  int n_ent;                                 // entries of the routed experts
   int tok_n[kSmMaxT];                        // pairs of each token
   int tok_pair[kSmMaxT * (kMaxTopK + 1)];    // their indices, ascending
   float sgate[kSmMaxT];
@@ -107,14 +110,15 @@ ES_DEV void small_stage_x(const SmallArgs& a, uint16_t* xs, float* xsum, int tid
 }
 
 // Route: the T tokens (warp t routes token t) or read the given
-// routing while the warps from kSmMaxT up stage x, and list the pairs in
+// routing while the warps from kRouteWarps up stage x, and list the pairs in
 // (expert id, token, slot) order.
 template <int VPL>
 ES_DEV void small_route(const SmallArgs& a, SmallState& st, uint16_t* xs, float* xsum) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int k = a.k, T = a.T;
-  if (warp < T) {
-    const int t = warp;
+  if (threadIdx.x == 0) st.n_ent = 0;
+  if (warp < kRouteWarps) {
+   for (int t = warp; t < T; t += kRouteWarps) {
     int my_e = -1;
     float my_w = 0.f;
     if (a.logits) {
@@ -140,73 +144,85 @@ ES_DEV void small_route(const SmallArgs& a, SmallState& st, uint16_t* xs, float*
       const float gs = shared_gate_warp(a.x + (size_t)t * a.D, a.sg_w, a.D);
       if (lane == 0) st.sgate[t] = gs;
     }
-  } else if (warp >= kSmMaxT) {
-    small_stage_x(a, xs, xsum, kSmMaxT * 32);
+   }
+  } else {
+    small_stage_x(a, xs, xsum, kRouteWarps * 32);
   }
   __syncthreads();
-  // one thread per slot: whether it is the first slot of its expert, then
-  // its rank among the valid slots by (expert, slot index) -- its pair
-  // index -- and, for a first slot, the expert's entry; and its place in
-  // its token's own pair list (ascending expert id)
+  // One thread per slot: its pair index (rank among the valid slots by
+  // (expert, slot index)), its expert's slot count and its place among them.
+  // An expert's pairs form entries of at most kSmallEntryPairs pairs (the
+  // 8 columns of an m16n8 tile); an expert's first slot records how many.
   constexpr int S = kMaxTopK + 1;
+  constexpr int EP = kSmallEntryPairs;
   const int ns = T * k;
   const int s = threadIdx.x;
   const bool valid = s < ns && st.slot_e[s] >= 0;
-  bool first = valid;
-  if (valid)
-    for (int s2 = 0; s2 < s; ++s2)
-      if (st.slot_e[s2] == st.slot_e[s]) { first = false; break; }
-  if (s < ns) st.first[s] = first ? 1 : 0;
-  const int n_routed = __syncthreads_count(valid);
-  const int n_first = __syncthreads_count(first);
+  int rank = 0, cnt_same = 0, wpos = 0;
   if (valid) {
-    const int e = st.slot_e[s], t = s / k;
-    int rank = 0, first_rank = 0, cnt_same = 0;
+    const int e = st.slot_e[s];
 #pragma unroll 8
     for (int s2 = 0; s2 < ns; ++s2) {
       const int e2 = st.slot_e[s2];
-      const bool v2 = e2 >= 0;
-      rank += (v2 && (e2 < e || (e2 == e && s2 < s))) ? 1 : 0;
+      rank += (e2 >= 0 && (e2 < e || (e2 == e && s2 < s))) ? 1 : 0;
       cnt_same += e2 == e;
-      first_rank += (v2 && e2 < e && st.first[s2]) ? 1 : 0;
+      wpos += (e2 == e && s2 < s) ? 1 : 0;
+    }
+  }
+  const int n_entries_here = (valid && wpos == 0) ? (cnt_same + EP - 1) / EP : 0;
+  if (s < ns) st.ent[s] = n_entries_here;
+  if (n_entries_here) atomicAdd(&st.n_ent, n_entries_here);
+  const int n_routed = __syncthreads_count(valid);
+  // entry of each pair: the entries of the lower experts, then wpos / EP;
+  // and the pair's place in its token's own list (ascending expert id)
+  if (valid) {
+    const int e = st.slot_e[s], t = s / k;
+    int ubase = 0;
+#pragma unroll 8
+    for (int s2 = 0; s2 < ns; ++s2) {
+      const int e2 = st.slot_e[s2];
+      ubase += (e2 >= 0 && e2 < e) ? st.ent[s2] : 0;
     }
     int tpos = 0;
     for (int j = 0; j < k; ++j) {
       const int s2 = t * k + j, e2 = st.slot_e[s2];
       tpos += (e2 >= 0 && (e2 < e || (e2 == e && s2 < s))) ? 1 : 0;
     }
+    const int u = ubase + wpos / EP;
     st.pair_tok[rank] = t;
     st.pair_w[rank] = st.slot_w[s];
-    st.pair_u[rank] = first_rank;
+    st.pair_u[rank] = u;
     st.tok_pair[t * S + tpos] = rank;
-    if (first) {
-      st.act_e[first_rank] = e;
-      st.act_off[first_rank] = rank;
-      st.act_n[first_rank] = cnt_same;
+    if (wpos % EP == 0) {
+      st.act_e[u] = e;
+      st.act_off[u] = rank;
+      st.act_n[u] = min(EP, cnt_same - wpos);
     }
   }
   // one thread per token: its pair count, and its shared-expert pair (the
-  // last entry, after every routed expert)
+  // last of its list, after every routed expert); the shared expert's pairs
+  // form entries of EP tokens each
+  const int n_ent = st.n_ent;
   if (s < T) {
     int nv = 0;
     for (int j = 0; j < k; ++j) nv += st.slot_e[s * k + j] >= 0 ? 1 : 0;
     if (a.has_shared) {
-      const int p = n_routed + s;
+      const int p = n_routed + s, u = n_ent + s / EP;
       st.pair_tok[p] = s;
       st.pair_w[p] = st.sgate[s];
-      st.pair_u[p] = n_first;
+      st.pair_u[p] = u;
       st.tok_pair[s * S + nv] = p;
       ++nv;
+      if (s % EP == 0) {
+        st.act_e[u] = a.E;
+        st.act_off[u] = p;
+        st.act_n[u] = min(EP, T - s);
+      }
     }
     st.tok_n[s] = nv;
   }
   if (s == 0) {
-    if (a.has_shared) {
-      st.act_e[n_first] = a.E;
-      st.act_off[n_first] = n_routed;
-      st.act_n[n_first] = T;
-    }
-    st.n_act = n_first + (a.has_shared ? 1 : 0);
+    st.n_act = n_ent + (a.has_shared ? (T + EP - 1) / EP : 0);
     st.n_pairs = n_routed + (a.has_shared ? T : 0);
   }
   __syncthreads();
@@ -558,8 +574,11 @@ bool small_path_fits(int T, int D, int I, int E, int k, int has_shared) {
 }
 
 cudaError_t launch_small(SmallArgs a, cudaStream_t st) {
-  a.ks_gu = share_count(a.D / kGroup, kMaxSplitK);
-  a.ks_dn = share_count(a.I / kGroup, kMaxSplitK);
+  // above kSplitKMaxTokens tokens: up to twice the entries, half the shares,
+  // so the partials fit the same workspace
+  const int cap = a.T > kSplitKMaxTokens ? kSmallSplitKLarge : kMaxSplitK;
+  a.ks_gu = share_count(a.D / kGroup, cap);
+  a.ks_dn = share_count(a.I / kGroup, cap);
   const int vpl = (a.E + 31) / 32;
   if (vpl <= 1) return launch_small_vpl<1>(a, st);
   if (vpl <= 2) return launch_small_vpl<2>(a, st);

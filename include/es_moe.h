@@ -83,7 +83,7 @@ typedef struct es_moe_cfg {
                            *       expert) pairs per routed expert
                            *       p = T * top_k / num_experts: with
                            *       T >= 64, path 2 for p > 48, path 3 for
-                           *       4 <= p <= 48; path 4 for T <= 8; the
+                           *       4 <= p <= 48; path 4 for T <= 16; the
                            *       decode path otherwise (path 3 for fp16
                            *       x);
                            *   1 = decode path (register-operand GEMV on the
@@ -94,10 +94,10 @@ typedef struct es_moe_cfg {
                            *   3 = tensor-core path with 32-token tiles and
                            *       the dequantised weights in tensor memory
                            *       (same arithmetic as 2);
-                           *   4 = the fused tiny-batch kernel (T <= 8, bf16
+                           *   4 = the fused tiny-batch kernel (T <= 16, bf16
                            *       x): the whole block in one cooperative
                            *       launch, decode-path arithmetic; path 0
-                           *       takes it for T <= 8 with bf16 x; larger
+                           *       takes it for T <= 16 with bf16 x; larger
                            *       batches given path 4 run the decode path */
   int32_t x_dtype;        /* activations x: ES_DTYPE_BF16 (0, the model
                            * dtype) or ES_DTYPE_F16 (the Expert Network's

@@ -124,16 +124,17 @@ def test_config_validation_in_python():
 def test_automatic_kernel_choice():
     """The automatic expert-FFN kernel rule (es_moe_cfg.kernel_path 0), by
     average pairs per routed expert p = T k / E: the fused tiny-batch kernel
-    for T <= 8, decode below 4, 32-token tensor tiles up to 48, 128-token
+    for T <= 16, decode below 4, 32-token tensor tiles up to 48, 128-token
     tiles above; tensor kernels from T = 64; fp16 activations never take the
     decode or fused kernels."""
     from expert_sniper_b200.block import ffn_kernels, uses_tensor_path
     q = PRESETS["qwen3-30b-a3b"]          # E = 128, k = 8
-    assert [ffn_kernels(q, T) for T in (1, 4, 5, 8, 9, 63, 64, 128, 256, 768, 769, 4096)] == [
-        "fused", "fused", "fused", "fused", "decode", "decode", "tensor-small", "tensor-small",
+    assert [ffn_kernels(q, T) for T in (1, 4, 5, 8, 16, 17, 63, 64, 128, 256, 768, 769, 4096)] == [
+        "fused", "fused", "fused", "fused", "fused", "decode", "decode", "tensor-small",
+        "tensor-small",
         "tensor-small", "tensor-small", "tensor", "tensor"]
-    assert ffn_kernels(q.with_(kernel_path="fused"), 8) == "fused"
-    assert ffn_kernels(q.with_(kernel_path="fused"), 9) == "decode"
+    assert ffn_kernels(q.with_(kernel_path="fused"), 16) == "fused"
+    assert ffn_kernels(q.with_(kernel_path="fused"), 17) == "decode"
     small = MoEConfig(256, 4, 2, 256, True)  # p = T / 2: the T >= 64 floor decides
     assert ffn_kernels(small, 32) == "decode" and ffn_kernels(small, 64) == "tensor-small"
     assert ffn_kernels(small, 98) == "tensor"

@@ -48,12 +48,15 @@ def test_block_bytes_counts_distinct_experts():
 def test_traffic_records_name_their_kernel_family():
     with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
         rec = json.load(f)
-    fams = {"decode", "tensor", "tensor-small"}
+    fams = {"decode", "tensor", "tensor-small", "fused"}
     for key, v in rec.items():
         model, t, fam, kernel = key.split(":")
         assert model in PRESETS and t.startswith("T") and fam in fams and kernel
-        # DRAM traffic within a few percent of the algorithmic bytes: no re-reads
-        assert 1.0 <= v["dram_bytes"] / v["algorithmic_bytes"] < 1.05
+        # DRAM traffic within a few percent of the algorithmic bytes: no
+        # re-reads (the fused kernel's split-K partials, a few MB per call,
+        # partly spill from L2: up to 10 % more)
+        limit = 1.10 if fam == "fused" else 1.05
+        assert 1.0 <= v["dram_bytes"] / v["algorithmic_bytes"] < limit
 
 
 def test_measured_peak():

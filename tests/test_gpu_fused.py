@@ -1,5 +1,5 @@
 """The fused tiny-batch kernel (es_small.cu, kernel_path "fused", the
-automatic choice for T <= 8) against the CPU oracle, through the C ABI:
+automatic choice for T <= 16) against the CPU oracle, through the C ABI:
 routing as in test_gpu_block.py, outputs within 3e-3 x RMS (the decode
 kernels' arithmetic: exact 4-bit weights, fp16 h), bitwise-repeatable calls,
 given routing with masked / duplicate / out-of-range ids, the shared expert,
@@ -51,13 +51,13 @@ def _check(cfg, T, bias, seed, dev):
     return blk, x, logits, cb
 
 
-@pytest.mark.parametrize("T", [1, 2, 3, 4, 5, 6, 7, 8])
+@pytest.mark.parametrize("T", [1, 2, 3, 4, 5, 6, 7, 8, 9, 12, 16])
 @pytest.mark.parametrize("bias", [False, True])
 def test_fused_small(cuda, T, bias):
     _check(SMALL, T, bias, seed=T, dev=cuda)
 
 
-@pytest.mark.parametrize("T", [1, 4, 8])
+@pytest.mark.parametrize("T", [1, 4, 8, 9, 16])
 def test_fused_shared_expert(cuda, T):
     _check(SHARED, T, True, seed=10 + T, dev=cuda)
 
@@ -65,7 +65,9 @@ def test_fused_shared_expert(cuda, T):
 @pytest.mark.parametrize("name,T", [("olmoe-1b-7b", 2), ("qwen3-30b-a3b", 1),
                                     ("qwen3-30b-a3b", 4), ("qwen3-next-80b-a3b", 3),
                                     ("qwen3-235b-a22b", 4), ("qwen3-30b-a3b", 8),
-                                    ("qwen3-next-80b-a3b", 6), ("qwen3-235b-a22b", 8)])
+                                    ("qwen3-next-80b-a3b", 6), ("qwen3-235b-a22b", 8),
+                                    ("qwen3-30b-a3b", 16), ("olmoe-1b-7b", 13),
+                                    ("qwen3-next-80b-a3b", 16), ("qwen3-235b-a22b", 16)])
 def test_fused_reference_shapes(cuda, name, T):
     _check(PRESETS[name], T, name == "qwen3-30b-a3b", seed=20 + T, dev=cuda)
 
@@ -93,12 +95,13 @@ def test_fused_given_routing_masked_duplicate_out_of_range(cuda):
     assert torch.count_nonzero(out[0]) == 0
 
 
-def test_fused_eight_tokens_one_expert(cuda):
-    """Every one of 8 tokens routed to expert 0 (the full 8 columns of one
-    expert's tiles) next to scattered slots, duplicates and masked ones."""
+@pytest.mark.parametrize("T", [8, 11, 16])
+def test_fused_all_tokens_one_expert(cuda, T):
+    """Every token routed to expert 0 (8 tokens fill the 8 columns of one
+    expert entry; 11 and 16 take two entries) next to scattered slots,
+    duplicates and masked ones."""
     cfg = SMALL.with_(kernel_path="fused")
     lay = synthetic_layer(cfg, seed=8, device=cuda)
-    T = 8
     x, _, _, _ = synthetic_inputs(cfg, T, seed=12, device=cuda)
     g = np.random.default_rng(4)
     idx = np.stack([g.choice(np.arange(1, cfg.num_experts), cfg.top_k, replace=False)
@@ -125,7 +128,7 @@ def test_one_workspace_across_batch_sizes(cuda):
     packed = MoEBlock(cfg, weights=lay, max_tokens=1).packed
     ws = MoEBlock.new_workspace(cfg, 64, cuda)
     for T, path in [(64, "auto"), (1, "auto"), (8, "fused"), (64, "auto"), (3, "decode"),
-                    (4, "auto"), (2, "fused")]:
+                    (16, "auto"), (4, "auto"), (12, "decode"), (2, "fused")]:
         x, _, logits, _ = synthetic_inputs(cfg, T, seed=50 + T, device=cuda)
         big = MoEBlock(cfg.with_(kernel_path=path), packed=packed, max_tokens=64, workspace=ws)
         got = big.forward(x, logits, None, out_dtype=torch.float32)
