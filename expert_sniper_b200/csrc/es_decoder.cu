@@ -8,6 +8,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "es_moe.h"
 
 namespace {
@@ -30,22 +32,83 @@ __device__ __forceinline__ float block_sum(float v, float* s_warp) {
   return t;
 }
 
-// one block per row: h += delta (if any); out = h * rsqrt(mean(h^2) + eps) * w
+// one block per row: h += delta (if any); out = h * rsqrt(mean(h^2) + eps) * w.
+// Each thread takes 8-column chunks (16-byte loads) and keeps the rounded
+// residual of up to kNormChunks chunks in registers, so nothing is read back
+// from memory between the update and the norm.
+constexpr int kNormChunks = 4;
 __global__ void add_rmsnorm_kernel(uint16_t* h, const uint16_t* delta, const uint16_t* w,
                                    uint16_t* out, int cols, float eps) {
+  __shared__ float s_warp[32];
+  const size_t base = (size_t)blockIdx.x * cols;
+  const int n8 = cols / 8;
+  float r[kNormChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNormChunks; ++j) {
+    const int c8 = threadIdx.x + j * blockDim.x;
+    if (c8 < n8) {
+      const uint4 hv = *reinterpret_cast<const uint4*>(h + base + (size_t)c8 * 8);
+      const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+      uint32_t dw[4] = {0u, 0u, 0u, 0u};
+      if (delta) {
+        const uint4 dv = *reinterpret_cast<const uint4*>(delta + base + (size_t)c8 * 8);
+        dw[0] = dv.x; dw[1] = dv.y; dw[2] = dv.z; dw[3] = dv.w;
+      }
+      uint32_t ow[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float lo = bf((uint16_t)(hw[q] & 0xffffu)), hi = bf((uint16_t)(hw[q] >> 16));
+        if (delta) {
+          // the residual stream stays bf16, as the model's
+          lo = bf(to_bf(lo + bf((uint16_t)(dw[q] & 0xffffu))));
+          hi = bf(to_bf(hi + bf((uint16_t)(dw[q] >> 16))));
+        }
+        r[j][2 * q] = lo;
+        r[j][2 * q + 1] = hi;
+        ss += lo * lo + hi * hi;
+        ow[q] = (uint32_t)to_bf(lo) | ((uint32_t)to_bf(hi) << 16);
+      }
+      if (delta)
+        *reinterpret_cast<uint4*>(h + base + (size_t)c8 * 8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+  }
+  const float rs = rsqrtf(block_sum(ss, s_warp) / cols + eps);
+#pragma unroll
+  for (int j = 0; j < kNormChunks; ++j) {
+    const int c8 = threadIdx.x + j * blockDim.x;
+    if (c8 < n8) {
+      const uint4 wv = *reinterpret_cast<const uint4*>(w + (size_t)c8 * 8);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t ow[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float o0 = r[j][2 * q] * rs * bf((uint16_t)(ww[q] & 0xffffu));
+        const float o1 = r[j][2 * q + 1] * rs * bf((uint16_t)(ww[q] >> 16));
+        ow[q] = (uint32_t)to_bf(o0) | ((uint32_t)to_bf(o1) << 16);
+      }
+      *reinterpret_cast<uint4*>(out + base + (size_t)c8 * 8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+  }
+}
+
+// the same for rows that the vector form does not take (cols % 8, unaligned
+// or longer than kNormChunks chunks per thread): scalar, two passes
+__global__ void add_rmsnorm_scalar_kernel(uint16_t* h, const uint16_t* delta, const uint16_t* w,
+                                          uint16_t* out, int cols, float eps) {
   __shared__ float s_warp[32];
   const size_t base = (size_t)blockIdx.x * cols;
   float ss = 0.f;
   for (int c = threadIdx.x; c < cols; c += blockDim.x) {
     float v = bf(h[base + c]);
     if (delta) {
-      v += bf(delta[base + c]);
-      h[base + c] = to_bf(v);  // the residual stream stays bf16, as the model's
-      v = bf(h[base + c]);
+      v = bf(to_bf(v + bf(delta[base + c])));
+      h[base + c] = to_bf(v);
     }
     ss += v * v;
   }
   const float r = rsqrtf(block_sum(ss, s_warp) / cols + eps);
+  __syncthreads();
   for (int c = threadIdx.x; c < cols; c += blockDim.x)
     out[base + c] = to_bf(bf(h[base + c]) * r * bf(w[c]));
 }
@@ -213,10 +276,22 @@ es_status es_dec_add_rmsnorm(void* h, const void* delta, const void* weight, voi
                              int32_t rows, int32_t cols, float eps, es_stream_t stream) {
   if (!h || !weight || !out || rows < 0 || cols <= 0) return ES_ERR_INVALID_ARG;
   if (rows == 0) return ES_OK;
-  const int threads = cols >= 1024 ? 256 : 128;
-  add_rmsnorm_kernel<<<rows, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<uint16_t*>(h), static_cast<const uint16_t*>(delta),
-      static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), cols, eps);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uintptr_t al = reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(delta) |
+                       reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(out);
+  const int n8 = cols / 8;
+  // 8-column chunks: a thread per chunk up to 256 threads, up to
+  // kNormChunks chunks per thread
+  const int threads = std::min(256, ((n8 + 31) / 32) * 32);
+  if (cols % 8 == 0 && al % 16 == 0 && n8 <= threads * kNormChunks) {
+    add_rmsnorm_kernel<<<rows, threads, 0, st>>>(
+        static_cast<uint16_t*>(h), static_cast<const uint16_t*>(delta),
+        static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), cols, eps);
+  } else {
+    add_rmsnorm_scalar_kernel<<<rows, cols >= 1024 ? 256 : 128, 0, st>>>(
+        static_cast<uint16_t*>(h), static_cast<const uint16_t*>(delta),
+        static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), cols, eps);
+  }
   return cudaGetLastError() == cudaSuccess ? ES_OK : ES_ERR_CUDA;
 }
 

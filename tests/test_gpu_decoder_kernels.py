@@ -21,7 +21,8 @@ def _within_ulp(got, want):
     return bool(((g - w).abs() <= w.abs() * ULP + 1e-30).all())
 
 
-@pytest.mark.parametrize("rows,cols", [(1, 2048), (5, 256), (64, 2048), (3, 1000)])
+@pytest.mark.parametrize("rows,cols", [(1, 2048), (5, 256), (64, 2048), (3, 1000), (2, 4096),
+                                       (16, 2048), (4, 8192), (2, 9000), (1, 24)])
 @pytest.mark.parametrize("with_delta", [True, False])
 def test_add_rmsnorm(cuda, rows, cols, with_delta):
     g = torch.Generator(device=cuda).manual_seed(rows * cols)
