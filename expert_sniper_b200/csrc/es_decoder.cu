@@ -3,16 +3,24 @@
 // RMS norm, the per-head q/k RMS norm + rotary embedding + KV-cache write of
 // Qwen3 attention, and a weight-streaming GEMV for the projections at batch
 // 1-4. Plain kernels in fp32 arithmetic on bf16 tensors; no counterpart in
-// the reference beyond the MLX ops they replace.
+// the reference beyond the MLX ops they replace. All are launched as
+// programmatic dependents (each waits for the kernel before it, then lets
+// the next one launch), so a chain of them overlaps launch and ramp-up.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <algorithm>
 
+#include "es_common.cuh"
+#include "es_kernels.cuh"
 #include "es_moe.h"
 
 namespace {
+
+using es::launch_pdl;
+using es::pdl_trigger;
+using es::pdl_wait;
 
 __device__ __forceinline__ float bf(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
 __device__ __forceinline__ uint16_t to_bf(float f) {
@@ -40,6 +48,8 @@ constexpr int kNormChunks = 4;
 __global__ void add_rmsnorm_kernel(uint16_t* h, const uint16_t* delta, const uint16_t* w,
                                    uint16_t* out, int cols, float eps) {
   __shared__ float s_warp[32];
+  pdl_trigger();
+  pdl_wait();
   const size_t base = (size_t)blockIdx.x * cols;
   const int n8 = cols / 8;
   float r[kNormChunks][8];
@@ -97,6 +107,8 @@ __global__ void add_rmsnorm_kernel(uint16_t* h, const uint16_t* delta, const uin
 __global__ void add_rmsnorm_scalar_kernel(uint16_t* h, const uint16_t* delta, const uint16_t* w,
                                           uint16_t* out, int cols, float eps) {
   __shared__ float s_warp[32];
+  pdl_trigger();
+  pdl_wait();
   const size_t base = (size_t)blockIdx.x * cols;
   float ss = 0.f;
   for (int c = threadIdx.x; c < cols; c += blockDim.x) {
@@ -121,6 +133,8 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* qkv, const uint16_t* qn, 
                                        const float* cos_t, const float* sin_t, const int64_t* pos,
                                        uint16_t* q_out, uint16_t* kc, uint16_t* vc, int B, int H,
                                        int KV, int hd, int max_ctx, float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int heads = H + 2 * KV;
@@ -163,8 +177,11 @@ __global__ void qk_norm_rope_kv_kernel(const uint16_t* qkv, const uint16_t* qn, 
 // weight-streaming shape of a decode step at batch 1-4. One warp per
 // kGemvRows output rows; each lane reads 16-byte runs of the weight rows
 // (coalesced: a warp covers 256 consecutive columns of a row per load),
-// kGemvUnroll loads per row in flight before their use; the x vectors sit in
-// shared memory; fp32 accumulation, one warp reduction per (row, vector).
+// kGemvUnroll loads per row in flight, the next batch loading while the
+// current one is used; the x vectors sit in shared memory; fp32
+// accumulation, one warp reduction per (row, vector). Launched as a
+// programmatic dependent: the first weight loads are issued before waiting
+// for the kernel that writes x, so they stream while it finishes.
 constexpr int kGemvMaxB = 4;
 constexpr int kGemvRows = 2;
 constexpr int kGemvWarps = 8;
@@ -178,27 +195,45 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const uint16_t* _
   extern __shared__ uint4 s_x4[];  // [B][K / 8]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int k8 = K / 8;
+  const int n0 = (blockIdx.x * kGemvWarps + warp) * kGemvRows;
+  uint4 wv[2][kGemvUnroll][kGemvRows];
+  auto load = [&](int c0, uint4 (&dst)[kGemvUnroll][kGemvRows]) {
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; ++u)
+#pragma unroll
+      for (int r = 0; r < kGemvRows; ++r) {
+        const int c = c0 + 32 * u;
+        dst[u][r] = (c < k8 && n0 + r < N)
+                        ? __ldcs(reinterpret_cast<const uint4*>(w + (size_t)(n0 + r) * K) + c)
+                        : make_uint4(0, 0, 0, 0);
+      }
+  };
+  // weights do not depend on the previous kernel: start them first
+  load(lane, wv[0]);
+  if (32 * kGemvUnroll < k8) load(lane + 32 * kGemvUnroll, wv[1]);
+  pdl_trigger();
+  pdl_wait();
   for (int i = threadIdx.x; i < B * k8; i += blockDim.x)
     s_x4[i] = reinterpret_cast<const uint4*>(x)[i];
   __syncthreads();
-  const int n0 = (blockIdx.x * kGemvWarps + warp) * kGemvRows;
   if (n0 >= N) return;
   float acc[kGemvRows][B];
 #pragma unroll
   for (int r = 0; r < kGemvRows; ++r)
 #pragma unroll
     for (int b = 0; b < B; ++b) acc[r][b] = 0.f;
-  for (int c0 = lane; c0 < k8; c0 += 32 * kGemvUnroll) {
-    uint4 wv[kGemvUnroll][kGemvRows];
+  int cur = 0;
+  for (int c0 = lane; c0 < k8; c0 += 32 * kGemvUnroll, cur ^= 1) {
+    // the batch after next goes into the buffer this iteration frees
+    uint4 wc[kGemvUnroll][kGemvRows];
 #pragma unroll
     for (int u = 0; u < kGemvUnroll; ++u)
 #pragma unroll
-      for (int r = 0; r < kGemvRows; ++r) {
-        const int c = c0 + 32 * u;
-        wv[u][r] = (c < k8 && n0 + r < N)
-                       ? __ldcs(reinterpret_cast<const uint4*>(w + (size_t)(n0 + r) * K) + c)
-                       : make_uint4(0, 0, 0, 0);
-      }
+      for (int r = 0; r < kGemvRows; ++r) wc[u][r] = cur ? wv[1][u][r] : wv[0][u][r];
+    if (c0 + 64 * kGemvUnroll < k8) {
+      if (cur) load(c0 + 64 * kGemvUnroll, wv[1]);
+      else load(c0 + 64 * kGemvUnroll, wv[0]);
+    }
 #pragma unroll
     for (int u = 0; u < kGemvUnroll; ++u) {
       const int c = c0 + 32 * u;
@@ -209,7 +244,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const uint16_t* _
         const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
         for (int r = 0; r < kGemvRows; ++r) {
-          const uint32_t ws[4] = {wv[u][r].x, wv[u][r].y, wv[u][r].z, wv[u][r].w};
+          const uint32_t ws[4] = {wc[u][r].x, wc[u][r].y, wc[u][r].z, wc[u][r].w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             acc[r][b] = fmaf(__uint_as_float(ws[q] << 16), __uint_as_float(xs[q] << 16), acc[r][b]);
@@ -241,9 +276,8 @@ cudaError_t launch_gemv(const uint16_t* w, const uint16_t* x, uint16_t* y, int N
     if (e != cudaSuccess) return e;
   }
   const int rows_per_block = kGemvWarps * kGemvRows;
-  gemv_kernel<B><<<(N + rows_per_block - 1) / rows_per_block, kGemvWarps * 32, smem, st>>>(w, x, y,
-                                                                                           N, K);
-  return cudaGetLastError();
+  return launch_pdl(gemv_kernel<B>, dim3((N + rows_per_block - 1) / rows_per_block),
+                    dim3(kGemvWarps * 32), smem, st, w, x, y, N, K);
 }
 
 }  // namespace
@@ -284,13 +318,17 @@ es_status es_dec_add_rmsnorm(void* h, const void* delta, const void* weight, voi
   // kNormChunks chunks per thread
   const int threads = std::min(256, ((n8 + 31) / 32) * 32);
   if (cols % 8 == 0 && al % 16 == 0 && n8 <= threads * kNormChunks) {
-    add_rmsnorm_kernel<<<rows, threads, 0, st>>>(
-        static_cast<uint16_t*>(h), static_cast<const uint16_t*>(delta),
-        static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), cols, eps);
+    if (launch_pdl(add_rmsnorm_kernel, dim3(rows), dim3(threads), 0, st,
+                   static_cast<uint16_t*>(h), static_cast<const uint16_t*>(delta),
+                   static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), cols,
+                   eps) != cudaSuccess)
+      return ES_ERR_CUDA;
   } else {
-    add_rmsnorm_scalar_kernel<<<rows, cols >= 1024 ? 256 : 128, 0, st>>>(
-        static_cast<uint16_t*>(h), static_cast<const uint16_t*>(delta),
-        static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), cols, eps);
+    if (launch_pdl(add_rmsnorm_scalar_kernel, dim3(rows), dim3(cols >= 1024 ? 256 : 128), 0, st,
+                   static_cast<uint16_t*>(h), static_cast<const uint16_t*>(delta),
+                   static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(out), cols,
+                   eps) != cudaSuccess)
+      return ES_ERR_CUDA;
   }
   return cudaGetLastError() == cudaSuccess ? ES_OK : ES_ERR_CUDA;
 }
@@ -308,13 +346,14 @@ es_status es_dec_qk_norm_rope_kv(const void* qkv, const void* q_norm, const void
   if (batch == 0) return ES_OK;
   const int items = batch * (heads + 2 * kv_heads);
   const int warps = 8;
-  qk_norm_rope_kv_kernel<<<(items + warps - 1) / warps, warps * 32, 0,
-                           static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t*>(qkv), static_cast<const uint16_t*>(q_norm),
-      static_cast<const uint16_t*>(k_norm), cos_table, sin_table, pos,
-      static_cast<uint16_t*>(q_out), static_cast<uint16_t*>(k_cache),
-      static_cast<uint16_t*>(v_cache), batch, heads, kv_heads, head_dim, max_ctx, eps);
-  return cudaGetLastError() == cudaSuccess ? ES_OK : ES_ERR_CUDA;
+  return launch_pdl(qk_norm_rope_kv_kernel, dim3((items + warps - 1) / warps), dim3(warps * 32), 0,
+                    static_cast<cudaStream_t>(stream), static_cast<const uint16_t*>(qkv),
+                    static_cast<const uint16_t*>(q_norm), static_cast<const uint16_t*>(k_norm),
+                    cos_table, sin_table, pos, static_cast<uint16_t*>(q_out),
+                    static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), batch,
+                    heads, kv_heads, head_dim, max_ctx, eps) == cudaSuccess
+             ? ES_OK
+             : ES_ERR_CUDA;
 }
 
 }  // extern "C"
