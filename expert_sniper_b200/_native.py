@@ -82,6 +82,7 @@ _SIGNATURES = {
     "es_moe_forward_noalloc": (ctypes.c_int, [_CFG, _P, _P, _I32, _P, _P, _P, _P, _I32, _P, _P,
                                               _I32, _P]),
     "es_moe_read_error": (ctypes.c_int, [_P, _I32, ctypes.POINTER(ctypes.c_uint32), _P]),
+    "es_moe_noalloc_read_error": (ctypes.c_int, [_I32, ctypes.POINTER(ctypes.c_uint32), _P]),
     "es_dec_add_rmsnorm": (ctypes.c_int, [_P, _P, _P, _P, _I32, _I32, ctypes.c_float, _P]),
     "es_dec_qk_norm_rope_kv": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32,
                                               _I32, _I32, _I32, ctypes.c_float, _P]),

@@ -24,8 +24,9 @@
 //     there; the counters that must start at zero are cleared at the start of
 //     each call, so calls that overlap on the GPU (different streams, or
 //     different host threads) race -- order them on one stream;
-//   - device-side error flags land in the shared scratch and are not
-//     reported by this entry point;
+//   - device-side error flags land in the shared scratch; each call clears
+//     them first, and es_moe_noalloc_read_error reads those of the last call
+//     on the current device;
 //   - the counters are cleared with three cudaMemsetAsync calls per call
 //     (a few microseconds of launch work ahead of the block's kernels);
 //   - nothing here calls cudaMalloc, cudaFree or any allocating routine.
@@ -128,6 +129,14 @@ es_status es_moe_forward_noalloc(const es_moe_cfg* cfg, const void* x, const voi
     return ES_ERR_CUDA;
   return es_moe_forward(cfg, x, logits, logits_dtype, cache_bias, shared_gate_w, packed, out,
                         out_dtype, topk_idx, topk_w, T, ws, kNoallocScratchBytes, stream);
+}
+
+es_status es_moe_noalloc_read_error(int32_t clear, uint32_t* flags_out, es_stream_t stream) {
+  if (!flags_out) return ES_ERR_INVALID_ARG;
+  void* ws = nullptr;
+  const es_status s = scratch_in_current_context(&ws);
+  if (s != ES_OK) return s;
+  return es_moe_read_error(ws, clear, flags_out, stream);
 }
 
 }  // extern "C"

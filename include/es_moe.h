@@ -327,7 +327,7 @@ ES_API es_status es_ep_combine_p2p(const es_ep_plan* plan, const int32_t* topk_i
  * 64 MiB returns ES_ERR_WORKSPACE. The first call on a device resolves the
  * array's address (make it before any stream capture on that device). All
  * calls on a device share the array: order them on one stream, since calls
- * that overlap on the GPU race. Device error flags are not reported here.
+ * that overlap on the GPU race. Device error flags: es_moe_noalloc_read_error.
  * No counterpart in the reference (an addition of this library). */
 ES_API es_status es_moe_forward_noalloc(const es_moe_cfg* cfg, const void* x,
                                         const void* logits, int32_t logits_dtype,
@@ -337,6 +337,12 @@ ES_API es_status es_moe_forward_noalloc(const es_moe_cfg* cfg, const void* x,
                                         int32_t out_dtype, int32_t* topk_idx,
                                         float* topk_w, int32_t T,
                                         es_stream_t stream);
+
+/* The device error word (ES_DEVERR_* bits) of the last
+ * es_moe_forward_noalloc call on the current device: each call clears it
+ * first. Blocks the host on `stream`; clears it when `clear` != 0. */
+ES_API es_status es_moe_noalloc_read_error(int32_t clear, uint32_t* flags_out,
+                                           es_stream_t stream);
 
 /* Synchronously read (and clear when `clear` != 0) the device error word of
  * a workspace. Blocks the host on `stream`. When ES_DEVERR_TIMEOUT is set by

@@ -62,3 +62,31 @@ def test_noalloc_rejects_batches_beyond_its_scratch(cuda):
         dummy.data_ptr(), dummy.data_ptr(), 0, None, None, 4096,
         torch.cuda.current_stream().cuda_stream)
     assert st == 3  # ES_ERR_WORKSPACE, before any launch
+
+
+@pytest.mark.parametrize("T", [3, 40])
+def test_noalloc_reports_device_errors(cuda, T):
+    """A NaN router logit sets ES_DEVERR_NONFINITE_LOGIT in the scratch's
+    error word: es_moe_noalloc_read_error returns it (fused kernel at T = 3,
+    decode kernels at T = 40), clears it on request, and the next clean call
+    starts from zero."""
+    cfg = MoEConfig(512, 32, 4, 512, True)
+    lay = synthetic_layer(cfg, seed=33, device=cuda)
+    blk = MoEBlock(cfg, weights=lay, max_tokens=T)
+    x, _, logits, _ = synthetic_inputs(cfg, T, seed=50, device=cuda)
+    bad = logits.clone()
+    bad[0, 3] = float("nan")
+    lib = _native.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    flags = ctypes.c_uint32(0)
+
+    def read(clear):
+        _native.check("es_moe_noalloc_read_error",
+                      lib.es_moe_noalloc_read_error(clear, ctypes.byref(flags), stream))
+        return flags.value
+
+    _noalloc(blk, x, bad, None)
+    assert read(1) & _native.DEVERR_NONFINITE_LOGIT
+    assert read(0) == 0
+    _noalloc(blk, x, logits, None)
+    assert read(0) == 0
