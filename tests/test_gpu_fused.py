@@ -95,6 +95,26 @@ def test_fused_given_routing_masked_duplicate_out_of_range(cuda):
     assert torch.count_nonzero(out[0]) == 0
 
 
+@pytest.mark.parametrize("T", [2, 13])
+def test_fused_f32_logits_match_decode_kernels(cuda, T):
+    """fp32 router logits (the dtype biased MLX logits promote to) through
+    the fused kernel: the same top-k and weights as the decode kernels, and
+    outputs within the parity tolerance of them."""
+    cfg = PRESETS["qwen3-30b-a3b"]
+    lay = synthetic_layer(cfg, seed=61, device=cuda)
+    x, _, logits, _ = synthetic_inputs(cfg, T, seed=62, device=cuda)
+    lg32 = logits.float() + 0.01 * torch.randn(logits.shape, device=cuda)
+    cb = cache_bias_vector(cfg.num_experts, 0.5, 7)[0].to(cuda)
+    fused = MoEBlock(cfg.with_(kernel_path="fused"), weights=lay, max_tokens=T)
+    dec = MoEBlock(cfg.with_(kernel_path="decode"), packed=fused.packed, max_tokens=T)
+    o1, i1, w1 = fused.forward(x, lg32, cb, out_dtype=torch.float32, return_routing=True)
+    o2, i2, w2 = dec.forward(x, lg32, cb, out_dtype=torch.float32, return_routing=True)
+    torch.cuda.synchronize()
+    assert fused.read_device_error() == 0 and dec.read_device_error() == 0
+    assert torch.equal(i1, i2) and torch.equal(w1, w2)
+    assert_close_rms(o1.cpu().numpy(), o2.cpu().numpy(), rel=FUSED_REL, what=f"f32 logits T={T}")
+
+
 @pytest.mark.parametrize("T", [8, 11, 16])
 def test_fused_all_tokens_one_expert(cuda, T):
     """Every token routed to expert 0 (8 tokens fill the 8 columns of one
