@@ -513,32 +513,67 @@ def run_ours_single(args):
                            kb=kb, clocks=clk, xs=xs, lgs=lgs, outs=outs, path=path_c,
                            dist=dist_ms)
 
-    # e2e through the public API with host buffers
+    # e2e through the public API with host buffers: every step copies its x
+    # and logits from pinned host memory and reads its output back. The
+    # copies run on a second stream, double-buffered, so step s + 1's inputs
+    # travel while step s's kernels run (a serving loop's overlap); events
+    # order each buffer's reuse.
     r = results[T]
     xs_h = [x.cpu().pin_memory() for x in r["xs"]]
     lg_h = [g.cpu().pin_memory() for g in r["lgs"]]
-    out_h = torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty_like(r["xs"][0])
-    ld = torch.empty_like(r["lgs"][0])
-    od = torch.empty((T, cfg.hidden), dtype=torch.bfloat16, device=dev)
+    out_h = [torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    xd = [torch.empty_like(r["xs"][0]) for _ in range(2)]
+    ld = [torch.empty_like(r["lgs"][0]) for _ in range(2)]
+    od = [torch.empty((T, cfg.hidden), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    copy = torch.cuda.Stream(dev)
     K_e2e = min(args.steps, 2000)
-    with torch.cuda.stream(stream):
-        def e2e_step(s):
-            l = s % L
-            xd.copy_(xs_h[l], non_blocking=True)
-            ld.copy_(lg_h[l], non_blocking=True)
-            blocks[l].forward(xd, ld, bias, out=od)
-            out_h.copy_(od, non_blocking=True)
-        for s in range(max(3, args.warmup)):
-            e2e_step(s)
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for s in range(K_e2e):
-            e2e_step(s)
-        e1.record(stream)
-        e1.synchronize()
+    ev = lambda: torch.cuda.Event()   # noqa: E731 (ordering only)
+    in_ready, fwd_done, out_done = {}, {}, {}
+
+    def h2d(s):
+        b = s % 2
+        if s - 2 in fwd_done:
+            copy.wait_event(fwd_done[s - 2])    # step s - 2 has read this buffer
+        with torch.cuda.stream(copy):
+            xd[b].copy_(xs_h[s % L], non_blocking=True)
+            ld[b].copy_(lg_h[s % L], non_blocking=True)
+            in_ready[s] = ev()
+            in_ready[s].record(copy)
+
+    def run(s):
+        b = s % 2
+        stream.wait_event(in_ready.pop(s))
+        if s - 2 in out_done:
+            stream.wait_event(out_done.pop(s - 2))   # step s - 2's output was read
+        with torch.cuda.stream(stream):
+            blocks[s % L].forward(xd[b], ld[b], bias, out=od[b])
+            fwd_done[s] = ev()
+            fwd_done[s].record(stream)
+        copy.wait_event(fwd_done[s])
+        with torch.cuda.stream(copy):
+            out_h[b].copy_(od[b], non_blocking=True)
+            out_done[s] = ev()
+            out_done[s].record(copy)
+        fwd_done.pop(s - 2, None)
+
+    def steps(n):
+        h2d(0)
+        for s in range(n):
+            if s + 1 < n:
+                h2d(s + 1)
+            run(s)
+
+    steps(max(3, args.warmup))
+    torch.cuda.synchronize()
+    in_ready.clear(); fwd_done.clear(); out_done.clear()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    copy.wait_stream(stream)
+    steps(K_e2e)
+    stream.wait_stream(copy)
+    e1.record(stream)
+    e1.synchronize()
     e2e_ms = e0.elapsed_time(e1) / K_e2e
 
     cpu = None
@@ -584,7 +619,9 @@ def run_ours_single(args):
         "step_ms_distribution": r["dist"],
         "e2e": {"value": T / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": T * cfg.hidden * 2 + T * cfg.num_experts * 2,
-                "d2h_bytes_per_step": T * cfg.hidden * 2, "ms_per_step": e2e_ms},
+                "d2h_bytes_per_step": T * cfg.hidden * 2, "ms_per_step": e2e_ms,
+                "copies": "pinned host buffers, double-buffered on a second stream: step s+1's "
+                          "inputs and step s-1's output move while step s's kernels run"},
         # per step: fused tiny-batch kernel 1; decode kernels front, gate/up,
         # down, combine; tensor-core kernels front, (scatter above 8192
         # slots), gate/up, down, combine
@@ -788,23 +825,56 @@ def run_ours_ep(args):
                                     device=dev)
         dist.all_reduce(acc, op=dist.ReduceOp.MAX)
         phases = {n: float(v) / n_rep for n, v in zip(names, acc.tolist())}
-    # e2e: host buffers in, host buffer out, through the same public path
+    # e2e: host buffers in, host buffer out, through the same public path;
+    # as on one GPU, the copies run on a second stream, double-buffered, so
+    # step s + 1's inputs travel while step s runs
     xs_h = [x.cpu().pin_memory() for x in xs]
     lg_h = [g.cpu().pin_memory() for g in lgs]
-    out_h = torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory()
-    xd, ld = torch.empty_like(xs[0]), torch.empty_like(lgs[0])
+    out_h = [torch.empty((T, cfg.hidden), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    xd = [torch.empty_like(xs[0]) for _ in range(2)]
+    ld = [torch.empty_like(lgs[0]) for _ in range(2)]
+    copy = torch.cuda.Stream(dev)
     K2 = min(K, 500)
+    in_ready, fwd_done, out_done = {}, {}, {}
+
+    def h2d(s):
+        bb = s % 2
+        if s - 2 in fwd_done:
+            copy.wait_event(fwd_done[s - 2])
+        with torch.cuda.stream(copy):
+            xd[bb].copy_(xs_h[s % L], non_blocking=True)
+            ld[bb].copy_(lg_h[s % L], non_blocking=True)
+            in_ready[s] = torch.cuda.Event()
+            in_ready[s].record(copy)
+
+    def run(s):
+        bb = s % 2
+        stream.wait_event(in_ready.pop(s))
+        if s - L in out_done:   # the layer's output buffer was read back
+            stream.wait_event(out_done.pop(s - L))
+        with torch.cuda.stream(stream):
+            b = backends[s % L]
+            o = b.step(xd[bb], ld[bb], bias) if p2p else ep.ep_forward(b, xd[bb], ld[bb], bias)
+            fwd_done[s] = torch.cuda.Event()
+            fwd_done[s].record(stream)
+        copy.wait_event(fwd_done[s])
+        with torch.cuda.stream(copy):
+            out_h[bb].copy_(o, non_blocking=True)
+            out_done[s] = torch.cuda.Event()
+            out_done[s].record(copy)
+        fwd_done.pop(s - 2, None)
+
     torch.cuda.synchronize()
     dist.barrier()
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for s in range(K2):
-            xd.copy_(xs_h[s % L], non_blocking=True)
-            ld.copy_(lg_h[s % L], non_blocking=True)
-            b = backends[s % L]
-            o = b.step(xd, ld, bias) if p2p else ep.ep_forward(b, xd, ld, bias)
-            out_h.copy_(o, non_blocking=True)
-        e1.record(stream)
+    e0.record(stream)
+    copy.wait_stream(stream)
+    h2d(0)
+    for s in range(K2):
+        if s + 1 < K2:
+            h2d(s + 1)
+        run(s)
+    stream.wait_stream(copy)
+    e1.record(stream)
     e1.synchronize()
     e2e_ms = torch.tensor([e0.elapsed_time(e1) / K2], device=dev)
     dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
@@ -845,7 +915,10 @@ def run_ours_ep(args):
                          "unit": "GB/s", "frac": achieved / peak, "traffic": None},
             "e2e": {"value": world * T / (float(e2e_ms.item()) * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": T * (cfg.hidden + cfg.num_experts) * 2,
-                    "d2h_bytes_per_step": T * cfg.hidden * 2},
+                    "d2h_bytes_per_step": T * cfg.hidden * 2,
+                    "copies": "pinned host buffers on every rank, double-buffered on a second "
+                              "stream: step s+1's inputs and step s-1's output move while step "
+                              "s runs"},
             # p2p: route, dispatch, receive, front, gate/up, down, combine (FFN:
             # front + 2 GEMMs + combine, or front + scatter + 2 + combine on the
             # tensor-core kernels), return, combine_p2p
