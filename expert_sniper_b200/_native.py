@@ -18,6 +18,7 @@ ES_OK = 0
 ES_DTYPE_BF16, ES_DTYPE_F16, ES_DTYPE_F32 = 0, 1, 2
 DEVERR_BAD_EXPERT_ID = 0x1
 DEVERR_NONFINITE_LOGIT = 0x2
+DEVERR_CAPACITY = 0x4
 DEVERR_TIMEOUT = 0x8
 DEVERR_RANGE = 0x10
 

@@ -200,7 +200,7 @@ es_status run_small(const es_moe_cfg* cfg, const Workspace& w, const es::RouteAr
   a.T = r.T; a.D = cfg->hidden; a.E = cfg->num_experts; a.k = cfg->top_k; a.I = cfg->inter;
   a.renorm = r.renorm; a.has_shared = r.has_shared;
   a.out = out; a.out_f32 = out_f32; a.out_idx = r.out_idx; a.out_w = r.out_w;
-  a.part = w.partials; a.h16 = w.h16;
+  a.part = w.partials; a.part_slots = (long long)w.part_slots; a.h16 = w.h16;
   // the counter region is zero between calls on every path
   a.ctr = w.counters; a.err = w.err;
   if (mk.mark(0, st) != cudaSuccess) return ES_ERR_CUDA;

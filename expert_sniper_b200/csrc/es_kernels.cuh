@@ -146,6 +146,7 @@ struct SmallArgs {
   size_t expert_bytes;
   int T, D, E, k, I, renorm, has_shared;
   int ks_gu, ks_dn;         // K shares of the gate/up and down items
+  long long part_slots;     // 2 KB slots in `part` (capacity check)
   void* out;
   int out_f32;
   int32_t* out_idx;         // [T][k] or null

@@ -122,6 +122,7 @@ struct Workspace {
   // `err`, the token bitmaps (tensor-core path: slot counters) from
   // `bitmap`, the split-K arrival counters from `counters`
   size_t zero_ctl_bytes, zero_bitmap_bytes, zero_counter_bytes;
+  size_t part_slots;   // 2 KB split-K slots in `partials`
 };
 
 // Carve (or, with base == nullptr, just size) the workspace for T tokens.
@@ -190,6 +191,7 @@ inline Workspace carve_workspace(void* base, int D, int E, int k, int I,
   const size_t dn_slots = shares * (D / 64);
   const size_t part_items = gu_slots > dn_slots ? gu_slots : dn_slots;
   size_t o_part = take(part_items * 512 * 4);
+  w.part_slots = part_items;
   w.bytes = off;
   w.zero_ctl_bytes = o_cnt - o_err;
   w.zero_bitmap_bytes = (size_t)E1 * W * 4;

@@ -47,6 +47,7 @@ constexpr int kSmMaxT = kSmallMaxTokens;
 constexpr int kRouteWarps = 8;  // warps that route (token t: warp t % 8); the rest stage x
 static_assert(kRouteWarps < kSmWarps, "routing warps and staging warps are disjoint");
 constexpr int kSmMaxPairs = kSmMaxT * kMaxTopK + kSmMaxT;  // routed + shared
+constexpr uint32_t kErrCapacity = 0x4u;
 constexpr uint32_t kErrTimeout = 0x8u;
 constexpr uint32_t kErrRange = 0x10u;
 
@@ -501,6 +502,24 @@ __global__ void __launch_bounds__(kSmThreads, 1) small_block_kernel(SmallArgs a)
   const int gw = warp * gridDim.x + blockIdx.x, nw = gridDim.x * kSmWarps;
   small_route<VPL>(a, st, xs, xsum);
   const int RP = a.I / 32, RQ = a.D / 64;
+  // The partials are sized for the entries routing can make. Given routing
+  // that repeats an expert inside a token's slots can cut more entries than
+  // that: then the call reports ES_DEVERR_CAPACITY and writes zeros (every
+  // CTA sees the same lists, so all take this path together).
+  {
+    const long long need_gu = (long long)st.n_act * RP * a.ks_gu;
+    const long long need_dn = (long long)st.n_act * RQ * a.ks_dn;
+    if (need_gu > a.part_slots || need_dn > a.part_slots) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) set_error(a.err, kErrCapacity);
+      const size_t n_out = (size_t)a.T * a.D;
+      for (size_t i = (size_t)blockIdx.x * kSmThreads + threadIdx.x; i < n_out;
+           i += (size_t)gridDim.x * kSmThreads) {
+        if (a.out_f32) static_cast<float*>(a.out)[i] = 0.f;
+        else static_cast<uint16_t*>(a.out)[i] = 0;
+      }
+      return;
+    }
+  }
   // phase 1: gate/up partials
   {
     const int items = st.n_act * RP * a.ks_gu;

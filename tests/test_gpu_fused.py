@@ -115,6 +115,39 @@ def test_fused_f32_logits_match_decode_kernels(cuda, T):
     assert_close_rms(o1.cpu().numpy(), o2.cpu().numpy(), rel=FUSED_REL, what=f"f32 logits T={T}")
 
 
+def test_fused_reports_capacity_for_repeated_experts(cuda):
+    """Given routing that repeats one expert 17 times across 8 tokens (a
+    token listing it in several slots) cuts more expert entries than the
+    partials hold at this shape: the call sets ES_DEVERR_CAPACITY and writes
+    zeros instead of running past the workspace, and the next call on the
+    same workspace is exact again."""
+    cfg = MoEConfig(512, 16, 4, 512, True, name="dup", kernel_path="fused")
+    lay = synthetic_layer(cfg, seed=71, device=cuda)
+    T = 8
+    x, _, _, _ = synthetic_inputs(cfg, T, seed=72, device=cuda)
+    idx = np.zeros((T, cfg.top_k), dtype=np.int32)
+    others = iter(range(1, 16))
+    for t in range(4, T):
+        for j in range(cfg.top_k):
+            if not (t == 4 and j == 0):
+                idx[t, j] = next(others)
+    w = np.random.default_rng(5).random((T, cfg.top_k)).astype(np.float32)
+    blk = MoEBlock(cfg, weights=lay, max_tokens=T)
+    out = blk.expert_ffn(x, torch.from_numpy(idx).to(cuda), torch.from_numpy(w).to(cuda),
+                         out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert blk.read_device_error(clear=True) & _native.DEVERR_CAPACITY
+    assert torch.count_nonzero(out) == 0
+    ok_idx = np.stack([np.random.default_rng(t).choice(16, 4, replace=False)
+                       for t in range(T)]).astype(np.int32)
+    out2 = blk.expert_ffn(x, torch.from_numpy(ok_idx).to(cuda), torch.from_numpy(w).to(cuda),
+                          out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert blk.read_device_error() == 0
+    ref = mo.expert_ffn(x.float().cpu().numpy(), layer_to_numpy(lay), ok_idx, w)
+    assert_close_rms(out2.cpu().numpy(), ref, rel=FUSED_REL, what="after a capacity error")
+
+
 @pytest.mark.parametrize("T", [8, 11, 16])
 def test_fused_all_tokens_one_expert(cuda, T):
     """Every token routed to expert 0 (8 tokens fill the 8 columns of one
