@@ -84,6 +84,7 @@ _SIGNATURES = {
                                               _I32, _P]),
     "es_moe_read_error": (ctypes.c_int, [_P, _I32, ctypes.POINTER(ctypes.c_uint32), _P]),
     "es_moe_noalloc_read_error": (ctypes.c_int, [_I32, ctypes.POINTER(ctypes.c_uint32), _P]),
+    "es_moe_kernel_family": (ctypes.c_int, [_CFG, _I32, ctypes.POINTER(ctypes.c_int32)]),
     "es_dec_add_rmsnorm": (ctypes.c_int, [_P, _P, _P, _P, _I32, _I32, ctypes.c_float, _P]),
     "es_dec_qk_norm_rope_kv": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32,
                                               _I32, _I32, _I32, ctypes.c_float, _P]),

@@ -339,6 +339,15 @@ es_status es_moe_workspace_bytes(const es_moe_cfg* cfg, int32_t max_tokens, size
   return ES_OK;
 }
 
+es_status es_moe_kernel_family(const es_moe_cfg* cfg, int32_t T, int32_t* path_out) {
+  es_status s = check_cfg(cfg);
+  if (s != ES_OK) return s;
+  if (!path_out || T < 1 || T > 65535) return ES_ERR_INVALID_ARG;
+  static const int32_t kPath[4] = {1, 2, 3, 4};  // decode, 128-token, 32-token, fused
+  *path_out = kPath[ffn_variant(cfg, T)];
+  return ES_OK;
+}
+
 es_status es_moe_route(const es_moe_cfg* cfg, const void* logits, int32_t logits_dtype,
                        const float* cache_bias, int32_t T, int32_t* topk_idx, float* topk_w,
                        es_stream_t stream) {

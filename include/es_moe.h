@@ -165,6 +165,12 @@ ES_API es_status es_moe_prepare_blocks(const es_moe_cfg* cfg, const void* blocks
 ES_API es_status es_moe_workspace_bytes(const es_moe_cfg* cfg, int32_t max_tokens,
                                  size_t* bytes_out);
 
+/* The expert-FFN kernel family a call with T tokens runs under `cfg`, as
+ * an es_moe_cfg.kernel_path value (1 decode, 2 128-token tensor-core
+ * tiles, 3 32-token tiles, 4 fused one-launch): the automatic rule applied,
+ * or the path cfg names. Host-only; needs no GPU. */
+ES_API es_status es_moe_kernel_family(const es_moe_cfg* cfg, int32_t T, int32_t* path_out);
+
 /* Router: logits (+ optional additive cache bias, promoted to fp32) ->
  * softmax (fp32) -> top-k -> optional renormalisation.
  *   logits     [T, E] bf16 or f32 (logits_dtype)

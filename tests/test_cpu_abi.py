@@ -146,3 +146,28 @@ def test_automatic_kernel_choice():
     for path in ("decode", "tensor", "tensor-small"):
         assert ffn_kernels(q.with_(kernel_path=path), 64) == path
     assert not uses_tensor_path(q, 63) and uses_tensor_path(q, 64)
+
+
+def test_python_kernel_rule_matches_the_library():
+    """block.ffn_kernels (the Python mirror used for accounting and by the
+    expert-parallel wrapper) names the same kernel family as the library's
+    own rule (es_moe_kernel_family), for every preset, forced path,
+    activation dtype and a range of batch sizes."""
+    import ctypes
+
+    from expert_sniper_b200.block import ffn_kernels
+    lib = _native.lib()
+    names = {1: "decode", 2: "tensor", 3: "tensor-small", 4: "fused"}
+    out = ctypes.c_int32(0)
+    for cfg in list(PRESETS.values()) + [MoEConfig(256, 16, 4, 256, True),
+                                         MoEConfig(3072, 64, 8, 1024, True)]:
+        for path in ("auto", "decode", "tensor", "tensor-small", "fused"):
+            for xd in ("bf16", "f16"):
+                if xd == "f16" and path in ("decode", "fused"):
+                    continue
+                c = cfg.with_(kernel_path=path, x_dtype=xd)
+                cc = c.to_c()
+                for T in (1, 2, 5, 8, 9, 15, 16, 17, 32, 63, 64, 65, 128, 255, 1024, 4096):
+                    _native.check("es_moe_kernel_family",
+                                  lib.es_moe_kernel_family(ctypes.byref(cc), T, ctypes.byref(out)))
+                    assert names[out.value] == ffn_kernels(c, T), (c.name, path, xd, T)
