@@ -9,8 +9,9 @@
 // weight is the sigmoid gate).
 //
 // Phases (grid = one CTA per SM, all co-resident: cooperative launch):
-//   0  every CTA: route the T tokens (warp per token) while the other warps
-//      stage x in fragment order with 64-group sums in shared memory, then
+//   0  every CTA: route the T tokens (warp t % 8 routes token t) while the
+//      other warps stage x in fragment order with 64-group sums in shared
+//      memory, then
 //      list the distinct experts in ascending id with their (token, weight)
 //      pairs, cut into entries of at most 8 pairs (the n = 8 columns of an
 //      m16n8 MMA tile; an expert with more pairs takes several entries and
@@ -31,9 +32,9 @@
 //      expert id (the K shares of each in fixed order), then the shared
 //      expert; bf16 or fp32 out, 16-column tiles per CTA
 // All arithmetic is fixed-order, so results are bitwise repeatable. Every
-// barrier wait is bounded (about a second) and reports ES_DEVERR_TIMEOUT.
-#include <cooperative_groups.h>
-
+// barrier wait is bounded (about a second) and reports ES_DEVERR_TIMEOUT;
+// routing whose entries outgrow the split-K partials (experts repeated in
+// given routing) reports ES_DEVERR_CAPACITY and writes zeros.
 #include "es_common.cuh"
 #include "es_kernels.cuh"
 #include "es_route.cuh"
@@ -77,9 +78,11 @@ ES_DEV void grid_barrier(unsigned* bar, unsigned b, uint32_t* err) {
 // Shared-memory state of one CTA (identical in every CTA after phase 0).
 struct SmallState {
   int n_pairs, n_act;
-  int act_e[kSmMaxPairs];      // distinct experts, ascending (E = shared)
+  int act_e[kSmMaxPairs];      // expert entries: runs of at most 8 of an
+                               // expert's pairs, by ascending expert id
+                               // (E = the shared expert)
   int act_off[kSmMaxPairs];    // their first pair
-  int act_n[kSmMaxPairs];      // their pairs
+  int act_n[kSmMaxPairs];      // their pairs (1..8)
   int pair_tok[kSmMaxPairs];   // token of each pair
   float pair_w[kSmMaxPairs];   // its weight (shared expert: the sigmoid gate)
   int pair_u[kSmMaxPairs];     // its entry in act_*
