@@ -175,13 +175,17 @@ __global__ void __launch_bounds__(kFrontThreads) front_kernel(RouteArgs r, Dispa
     }
   }
 
-  // the last CTA dispatches
-  __threadfence();
+  // the last CTA dispatches. The block barrier orders every thread's writes
+  // before thread 0's fence and ticket (one fence per CTA, as in a grid
+  // sync); the last CTA's thread 0 fences again before its threads read.
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(d.ticket, 1) == (int)gridDim.x - 1;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_last = atomicAdd(d.ticket, 1) == (int)gridDim.x - 1;
+    if (s_last) __threadfence();
+  }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   dispatch_cta(d, s_off);
   __syncthreads();
   const int words = (E + (r.has_shared ? 1 : 0)) * r.W;

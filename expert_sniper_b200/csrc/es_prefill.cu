@@ -335,13 +335,18 @@ __global__ void __launch_bounds__(kFrontThreads) pf_front_kernel(RouteArgs r, Pf
     x_row_to_f16(xv, r.x_perm + (size_t)t * r.D, r.xsum + t, r.D, r.x_f16 != 0);
   }
 
-  // the last CTA turns the counts into offsets and the active list
-  __threadfence();
+  // the last CTA turns the counts into offsets and the active list. The
+  // block barrier orders every thread's writes before thread 0's fence and
+  // ticket (one fence per CTA, as in a grid sync); the last CTA's thread 0
+  // fences again before its threads read.
   __syncthreads();
-  if (tid == 0) s_last = atomicAdd(d.ticket, 1) == (int)gridDim.x - 1;
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(d.ticket, 1) == (int)gridDim.x - 1;
+    if (s_last) __threadfence();
+  }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   const int E1 = E + (r.has_shared ? 1 : 0);
   for (int e = tid; e < E1; e += kFrontThreads) {
     s_off[e] = e < E ? __ldcg(d.cnt + e) : r.T;
