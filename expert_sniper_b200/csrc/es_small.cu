@@ -35,6 +35,8 @@
 // barrier wait is bounded (about a second) and reports ES_DEVERR_TIMEOUT;
 // routing whose entries outgrow the split-K partials (experts repeated in
 // given routing) reports ES_DEVERR_CAPACITY and writes zeros.
+#include <atomic>
+
 #include "es_common.cuh"
 #include "es_kernels.cuh"
 #include "es_route.cuh"
@@ -565,14 +567,33 @@ int share_count(int n, int cap) {
 template <int VPL>
 cudaError_t launch_small_vpl(SmallArgs a, cudaStream_t st) {
   const size_t smem = (size_t)a.T * a.D * 2 + (size_t)a.T * (a.D / kGroup) * 4;
-  cudaError_t e = cudaFuncSetAttribute(small_block_kernel<VPL>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // The shared-memory opt-in and the one-CTA-per-SM check are made once per
+  // device for the largest size seen so far (a smaller call fits the same
+  // opt-in and the same residency), not on every launch. A launch refused
+  // after all (a new context on the device has no opt-in) makes them again
+  // and retries once.
+  constexpr int kMaxDev = 64;
+  static std::atomic<size_t> checked[kMaxDev];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, small_block_kernel<VPL>, kSmThreads,
-                                                    smem);
-  if (e != cudaSuccess) return e;
-  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  const bool cached = dev >= 0 && dev < kMaxDev &&
+                      smem <= checked[dev].load(std::memory_order_acquire);
+  if (!cached) {
+    e = cudaFuncSetAttribute(small_block_kernel<VPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, small_block_kernel<VPL>, kSmThreads,
+                                                      smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    if (dev >= 0 && dev < kMaxDev) {
+      size_t cur = checked[dev].load(std::memory_order_relaxed);
+      while (smem > cur && !checked[dev].compare_exchange_weak(cur, smem)) {
+      }
+    }
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(sm_count());
   cfg.blockDim = dim3(kSmThreads);
@@ -583,7 +604,13 @@ cudaError_t launch_small_vpl(SmallArgs a, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, small_block_kernel<VPL>, a);
+  e = cudaLaunchKernelEx(&cfg, small_block_kernel<VPL>, a);
+  if (e != cudaSuccess && cached) {
+    (void)cudaGetLastError();
+    checked[dev].store(0, std::memory_order_release);
+    return launch_small_vpl<VPL>(a, st);
+  }
+  return e;
 }
 
 }  // namespace
