@@ -220,4 +220,8 @@ CASES = [
      "input_seed": 25, "T": 4, "bias": 0.5, "cache_seed": 26, "scales": "bf16"},
     {"name": "qwen3_next_T4_shared_f16", "preset": "qwen3-next-80b-a3b", "layer_seed": 31,
      "input_seed": 32, "T": 4, "bias": 0.0, "scales": "f16"},
+    {"name": "qwen3_30b_T16_bias_bf16", "preset": "qwen3-30b-a3b", "layer_seed": 21,
+     "input_seed": 41, "T": 16, "bias": 0.5, "cache_seed": 42, "scales": "bf16"},
+    {"name": "olmoe_T16_f16", "preset": "olmoe-1b-7b", "layer_seed": 11, "input_seed": 43,
+     "T": 16, "bias": 0.0, "scales": "f16"},
 ]

@@ -34,6 +34,17 @@ from tests import _refexec as rx
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 BAR = {"f16": 1e-2, "bf16": 5e-2}
+# With unbiased bf16 logits the reference's routing weights stay bf16 (MLX's
+# softmax keeps its input dtype) while this build and the oracle keep them
+# in fp32: that rounding alone puts whole blocks up to ~1.1e-2 x RMS apart
+# (measured: olmoe_T16_f16). Block comparisons of such cases get this bar;
+# the expert FFN fed the reference's own scores keeps the plain one.
+BF16_SCORES_BLOCK_BAR = 2e-2
+
+
+def block_bar(m):
+    bar = BAR[m["scales"]]
+    return max(bar, BF16_SCORES_BLOCK_BAR) if m["scores_dtype"] == "bfloat16" else bar
 
 
 @functools.lru_cache(maxsize=None)
@@ -80,7 +91,7 @@ def _oracle_rel(name):
 @pytest.mark.parametrize("name", [c["name"] for c in rx.CASES])
 def test_oracle_against_reference_vectors(name):
     rel, m = _oracle_rel(name)
-    assert rel <= BAR[m["scales"]], f"{name}: oracle {rel:.3e} x RMS from the reference"
+    assert rel <= block_bar(m), f"{name}: oracle {rel:.3e} x RMS from the reference"
     # the distance recorded when the vectors were made
     assert abs(rel - m["oracle_block_rel"]) <= 1e-4 + 1e-2 * m["oracle_block_rel"]
     if m["scores_dtype"] == "float32" and m["scales"] == "f16":

@@ -35,6 +35,17 @@ pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 BAR = {"f16": 1e-2, "bf16": 5e-2}
+# With unbiased bf16 logits the reference's routing weights stay bf16 (MLX's
+# softmax keeps its input dtype) while this build and the oracle keep them
+# in fp32: that rounding alone puts whole blocks up to ~1.1e-2 x RMS apart
+# (measured: olmoe_T16_f16). Block comparisons of such cases get this bar;
+# the expert FFN fed the reference's own scores keeps the plain one.
+BF16_SCORES_BLOCK_BAR = 2e-2
+
+
+def block_bar(m):
+    bar = BAR[m["scales"]]
+    return max(bar, BF16_SCORES_BLOCK_BAR) if m["scores_dtype"] == "bfloat16" else bar
 
 
 @functools.lru_cache(maxsize=None)
@@ -88,7 +99,7 @@ def test_block_against_reference_vectors(cuda, name):
     err_blk = 0.0
     if keep.any():
         err_blk = float(np.abs(out.cpu().numpy()[rows][keep] - ref[keep]).max()) / rms
-    assert err_blk <= bar, f"{name} [{ffn_kernels(cfg, T)}]: block {err_blk:.3e} x RMS"
+    assert err_blk <= block_bar(m), f"{name} [{ffn_kernels(cfg, T)}]: block {err_blk:.3e} x RMS"
 
     err_ffn = float(np.abs(ffn.cpu().numpy()[rows] - ref).max()) / rms
     assert err_ffn <= bar, f"{name} [{ffn_kernels(cfg, T)}]: expert FFN {err_ffn:.3e} x RMS"
