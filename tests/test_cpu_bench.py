@@ -1,11 +1,13 @@
-"""bench.py's accounting on the CPU: the algorithmic bytes per kernel for
-each expert-FFN kernel family (the roofline numerators), the traffic
-records it scales, and the peak it divides by."""
+"""bench.py on the CPU: the algorithmic bytes per kernel for each
+expert-FFN kernel family (the roofline numerators), the traffic records it
+scales, the peak it divides by, and the reference arm's line."""
 from __future__ import annotations
 
 import importlib.util
 import json
 import os
+import subprocess
+import sys
 
 from expert_sniper_b200 import PRESETS
 
@@ -63,3 +65,28 @@ def test_measured_peak():
     b = _bench()
     hbm, kind = b.measured_peaks()
     assert kind in ("measured", "fallback") and hbm > 1000
+
+
+def _run_bench(env_extra, *args):
+    env = dict(os.environ, **env_extra)
+    return subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), *args],
+                          capture_output=True, text=True, env=env, timeout=600, cwd=ROOT)
+
+
+def test_reference_arm_prints_one_line_on_rank_zero_only():
+    """`bench.py --impl reference` (the reference's algorithm on the host
+    cores) under a multi-process launch: rank 0 prints one JSON line with
+    impl "reference", the workload's metric and a zero-copy e2e; any other
+    rank exits 0 without work or output."""
+    other = _run_bench({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"},
+                       "--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "0")
+    assert other.returncode == 0 and other.stdout.strip() == ""
+    zero = _run_bench({"RANK": "0", "WORLD_SIZE": "2", "LOCAL_RANK": "0"},
+                      "--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "0")
+    assert zero.returncode == 0, zero.stderr[-2000:]
+    lines = [l for l in zero.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["value"] > 0
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+    assert line["metric"] == _bench().METRIC
